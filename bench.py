@@ -1,0 +1,408 @@
+#!/usr/bin/env python
+"""Stream-frames/s of the streaming-transformer LM step (semantic-voice-local's STT / TTS
+language-model token loop) on B200s, one process per GPU.
+
+A step is one frame of the LM for every stream the GPU holds: embeddings, every layer (norm,
+QKV + RoPE + KV-ring write, sliding-window attention, out-proj, FFN) and the head with the
+greedy argmax, fed back on the device. Streams are independent, so N GPUs run N independent
+batches ("weak" scaling, no collective on the data path).
+
+  python bench.py [--config 2] [--gpus N --steps K --warmup W] [--impl ours|reference]
+
+The default workload is BASELINE config 2 (STT-1b, q8_0 weights, batch 1, 1000 frames).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "semantic-ai_b200"), str(ROOT / "oracle")]
+
+from svl import config as C  # noqa: E402
+from svl import synth  # noqa: E402
+
+CONFIGS = {
+    "1": dict(workload="stt-1b f32 batch 1 (BASELINE config 1)", preset="stt_1b", wdt="f32",
+              kv="f32", batch=1, frames=1000),
+    "2": dict(workload="stt-1b q8_0 batch 1 (BASELINE config 2)", preset="stt_1b", wdt="q8_0",
+              kv="f32", batch=1, frames=1000),
+    "3": dict(workload="stt-1b bf16 256 streams/GPU, staggered fills (BASELINE config 3)",
+              preset="stt_1b", wdt="bf16", kv="bf16", batch=256, frames=1000, stagger=750),
+    "4": dict(workload="stt-2.6b q4_1 batch 1 (BASELINE config 4)", preset="stt_2b6",
+              wdt="q4_1", kv="bf16", batch=1, frames=1500),
+    "4b": dict(workload="stt-2.6b q4_1 128 streams/GPU (BASELINE config 4)", preset="stt_2b6",
+               wdt="q4_1", kv="bf16", batch=128, frames=1500, stagger=375),
+}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def preset(name: str) -> C.SttConfig:
+    return getattr(C, name)()
+
+
+def gemv_launches(cfg: C.TransformerConfig, stt: C.SttConfig, batch: int) -> int:
+    """Kernel launches of one step, as the engine issues them (launch_gemv splits the streams
+    into chunks whose input rows fit in 200 KB of shared memory)."""
+    wt = {"f32": 0, "bf16": 1, "q8_0": 2, "q4_1": 3}[cfg.weight_dtype]
+
+    def chunks(k, quantised=True):
+        t = wt if (quantised or wt == 1) else 0
+        for nb in (8, 4, 2, 1):
+            sm = nb * k * 4 if t in (0, 1) else nb * k + nb * (k // 32) * 4 * (2 if t == 3 else 1)
+            if sm <= 200 * 1024:
+                return math.ceil(batch / nb)
+        return batch
+
+    d, qd = cfg.d_model, cfg.num_heads * cfg.head_dim
+    per_layer = chunks(d) + 1 + chunks(qd) + chunks(d) + chunks(cfg.ffn_hidden)
+    n = 1 + cfg.num_layers * per_layer + chunks(d)
+    n += stt.extra_heads_num_heads * chunks(d, False) + (1 if stt.extra_heads_num_heads else 0)
+    return n + 1
+
+
+def run_ours(args, spec, rank, world, local_rank):
+    import torch
+    from svl import LanguageModel
+    from svl import _lib
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+
+    stt = preset(spec["preset"])
+    cfg = stt.transformer(spec["wdt"], spec["kv"])
+    B, K, W = spec["batch"], args.steps, args.warmup
+    weights = synth.stt_weights(stt, cfg, seed=0)
+    model = LanguageModel(stt, cfg, weights, device=local_rank)
+    L = _lib.lib()
+    wbytes = model.weight_bytes
+
+    # Per-stream audio: global stream g draws from seed 1 + g; frame 0 sees the initial tokens.
+    g0 = rank * B
+    audio = synth.audio_tokens(stt, K + W, seed=1 + g0, streams=B)
+    rng = np.random.default_rng(2 + rank)
+    offsets = (rng.integers(0, spec["stagger"], size=B) if spec.get("stagger") else np.zeros(B, int))
+
+    stream = torch.cuda.Stream()
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+
+    def fresh_state():
+        st = model.init_state(B)
+        for b in range(B):
+            if offsets[b]:
+                # Position the stream at its fill level (len 0: the ring contents stand in for
+                # the history, so the attention reads exactly min(pos + 1, window) keys).
+                _lib.check(L.svl_state_import(st.handle, b, 0, None, None, 0, int(offsets[b])))
+        return st
+
+    def dev(a):
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int32)).to(f"cuda:{local_rank}")
+
+    a_dev = dev(audio)  # [frames][B][n_q]
+    for b in range(B):
+        if offsets[b] == 0:
+            a_dev[0, b] = stt.card
+    text = [torch.full((B,), stt.text_card, dtype=torch.int32, device=f"cuda:{local_rank}"),
+            torch.zeros(B, dtype=torch.int32, device=f"cuda:{local_rank}")]
+    row = B * stt.n_q * 4
+
+    def device_steps(st, first, n):
+        for i in range(n):
+            src, dst = text[i % 2], text[(i + 1) % 2]
+            _lib.check(L.svl_stt_step_device(model.handle, st.handle, B, ctypes.c_void_p(src.data_ptr()),
+                                             ctypes.c_void_p(a_dev.data_ptr() + (first + i) * row),
+                                             ctypes.c_void_p(dst.data_ptr()), None, sptr))
+
+    # Warm-up (also captures the step's CUDA graph), then a fresh state for the timed run.
+    st = fresh_state()
+    with torch.cuda.stream(stream):
+        device_steps(st, 0, W)
+    stream.synchronize()
+    st.close()
+    st = fresh_state()
+    text[0].fill_(stt.text_card)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        device_steps(st, W, K)
+        e1.record(stream)
+    stream.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local_rank}")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * B * K / (ms_max / 1000.0)
+    st.close()
+
+    # End to end through the host-buffer C-ABI call: H2D of the step's tokens and D2H of the
+    # argmax inside the timed region, every step.
+    st = fresh_state()
+    prev = np.full(B, stt.text_card, np.uint32)
+    aud = audio.copy()
+    for b in range(B):
+        if offsets[b] == 0:
+            aud[0, b] = stt.card
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(K):
+        prev = model.step(prev, aud[i], st)
+    e2e_s = time.perf_counter() - t0
+    t = torch.tensor([e2e_s], dtype=torch.float64, device=f"cuda:{local_rank}")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * B * K / float(t.item())
+    st.close()
+
+    # Roofline of the dominant kernel family, timed on its launching stream.
+    peaks, peak_kind = load_peaks()
+    kern = {}
+    st = fresh_state()
+    # Put every stream at its steady-state fill for the attention timing.
+    for b in range(B):
+        _lib.check(L.svl_state_import(st.handle, b, 0, None, None, 0,
+                                      int(min(offsets[b] + K, cfg.context or offsets[b] + K))))
+    for which, name in ((0, "gemv (all weight products of a step)"), (1, "attention (all layers)")):
+        nbytes = ctypes.c_int64()
+        iters = 20
+        with torch.cuda.stream(stream):
+            _lib.check(L.svl_profile_kernels(model.handle, st.handle, B, which, 3, sptr, ctypes.byref(nbytes)))
+            stream.synchronize()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            _lib.check(L.svl_profile_kernels(model.handle, st.handle, B, which, iters, sptr, ctypes.byref(nbytes)))
+            a1.record(stream)
+        stream.synchronize()
+        per = a0.elapsed_time(a1) / iters
+        kern[name] = {"ms_per_step": per, "bytes_per_step": nbytes.value,
+                      "gbs": nbytes.value / (per / 1e3) / 1e9}
+    st.close()
+    dom = max(kern, key=lambda k: kern[k]["ms_per_step"])
+    launches = gemv_launches(cfg, stt, B)
+    n_launch_dom = (cfg.num_layers * 4 + 1) if dom.startswith("gemv") else cfg.num_layers
+    traffic = None
+    tfile = ROOT / "profiles" / f"traffic_config{args.config}.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+    hbm = peaks["hbm_gbs"]
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(kern[dom]["gbs"], 1),
+                "peak": hbm, "unit": "GB/s", "frac": round(kern[dom]["gbs"] / hbm, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "traffic": traffic,
+                "launches_per_step": n_launch_dom,
+                "algorithmic_bytes_per_launch": kern[dom]["bytes_per_step"] // n_launch_dom}
+    # Step-level roofline: weights + KV read + KV written per step over HBM bandwidth.
+    kv = sum(C.kv_bytes_per_stream(cfg, int(min(o + K / 2, cfg.context or o + K))) for o in offsets) / 2
+    step_bytes = wbytes + kv + B * cfg.num_layers * 2 * cfg.num_kv_heads * cfg.head_dim * (2 if cfg.kv_dtype == "bf16" else 4)
+    step_frac = step_bytes / (ms_max / K / 1e3) / (hbm * 1e9)
+
+    out = {
+        "metric": "stream-frames/s", "value": round(value, 2), "unit": "stream-frames/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_max / K, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": spec["wdt"], "data": "synthetic (random-init N(0,0.02) weights seed 0, uniform audio tokens seed 1+stream)",
+        "config": {"workload": spec["workload"], "streams_per_gpu": B, "frames": K,
+                   "d_model": cfg.d_model, "layers": cfg.num_layers, "window": cfg.context,
+                   "kv_dtype": cfg.kv_dtype, "parallelism": f"{world} GPU(s) x {B} independent streams, no collective",
+                   "l2": f"inputs larger than L2: {wbytes / 1e9:.3f} GB of weights streamed per step"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "stream-frames/s",
+                "h2d_bytes_per_step": B * (1 + stt.n_q) * 4, "d2h_bytes_per_step": B * 4},
+        "gpu_launches": launches * K,
+        "roofline": roofline,
+        "step_roofline": {"bytes_per_step": int(step_bytes), "frac": round(step_frac, 4),
+                          "unit": "of measured HBM GB/s"},
+        "kernels": kern,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(spec, stt, cfg, weights, budget_s=args.cpu_seconds)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def cpu_baseline(spec, stt, cfg, weights, budget_s=15.0, frames_cap=None):
+    """The oracle (a C restatement of the reference CPU path) on the host's cores: stream 0 of
+    the workload from position 0, frames until the time budget is spent."""
+    import oracle as O
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    om = O.OracleModel(0, cfg, weights, stt=stt)
+    st = om.init_state()
+    audio = synth.audio_tokens(stt, 4096, seed=1)
+    prev = stt.text_card
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and (frames_cap is None or n < frames_cap):
+        a = np.full(stt.n_q, stt.card, np.uint32) if n == 0 else audio[n]
+        prev, _, _ = om.stt_step(prev, a, st)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "stream-frames/s", "cores": threads, "kind": "port",
+            "sample": f"{n} frames of one stream from position 0 ({spec['wdt']} weights, "
+                      f"{cfg.kv_dtype} KV), {dt:.1f} s on {threads} threads"}
+
+
+def run_reference(args, spec, rank):
+    """The reference's CPU implementation of the path: the oracle port (the Rust reference
+    cannot be built in this image), all host threads, bounded samples of the workload."""
+    if rank != 0:
+        return
+    stt = preset(spec["preset"])
+    cfg = stt.transformer(spec["wdt"], spec["kv"])
+    weights = synth.stt_weights(stt, cfg, seed=0)
+    import oracle as O
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    om = O.OracleModel(0, cfg, weights, stt=stt)
+    del weights
+    audio = synth.audio_tokens(stt, args.steps + args.warmup + 1, seed=1)
+    st = om.init_state()
+    prev = stt.text_card
+    for i in range(args.warmup):
+        a = np.full(stt.n_q, stt.card, np.uint32) if i == 0 else audio[i]
+        prev, _, _ = om.stt_step(prev, a, st)
+    # Each step: one stream-frame (the whole step at batch 1; a one-stream sample otherwise),
+    # stopping early once the time budget is spent.
+    n = 0
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        if time.perf_counter() - t0 > args.ref_seconds:
+            break
+        a = audio[args.warmup + i] if args.warmup + i > 0 else np.full(stt.n_q, stt.card, np.uint32)
+        prev, _, _ = om.stt_step(prev, a, st)
+        n += 1
+    dt = time.perf_counter() - t0
+    value = n / dt
+    out = {"metric": "stream-frames/s", "value": round(value, 3), "unit": "stream-frames/s",
+           "n_gpus": args.gpus, "steps": n, "warmup": args.warmup,
+           "ms_per_step": round(dt / max(n, 1) * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": spec["wdt"], "data": "synthetic",
+           "config": {"workload": spec["workload"], "streams_per_gpu": spec["batch"]},
+           "impl": "reference",
+           "cpu_baseline": {"value": round(value, 3), "unit": "stream-frames/s", "cores": threads,
+                            "kind": "port",
+                            "sample": f"{n} frames of one stream after {args.warmup} warm-up frames "
+                                      f"(C restatement of the reference CPU path; the Rust reference "
+                                      f"needs cargo and candle 0.11.1, absent here)"},
+           "e2e": {"value": round(value, 3), "unit": "stream-frames/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--ref-seconds", type=float, default=120.0)
+    args = ap.parse_args()
+    spec = CONFIGS[args.config]
+    if args.steps is None:
+        args.steps = spec["frames"]
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus > 1 and world == 1:
+        sys.exit("--gpus N > 1 runs under torchrun: python -m torch.distributed.run "
+                 "--nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N")
+    if args.impl == "reference":
+        run_reference(args, spec, rank)
+    else:
+        run_ours(args, spec, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

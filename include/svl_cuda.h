@@ -1,0 +1,197 @@
+/*
+ * svl_cuda.h — C ABI of the B200 (sm_100a) streaming language-model step.
+ *
+ * This is the drop-in boundary for semantic-voice-local's per-frame StreamingTransformer
+ * step (Kyutai STT LanguageModel, Pocket-TTS FlowLm) on `--device cuda`. Every entry point
+ * names the reference interface it replaces; paths are relative to
+ * crates/semantic-voice-local/src/ in semantiverse/semantic-ai.
+ *
+ * Conventions
+ *  - Plain pointers and sizes only. Host pointers unless the name ends in _device.
+ *  - Every call returns an svl_status; svl_last_error() holds the message of the last
+ *    failure on the calling thread. The codes mirror the reference's Error enum
+ *    (error.rs:2-31): CONFIG = Error::Config, INVALID_INPUT = Error::InvalidInput,
+ *    CUDA/OOM/TIMEOUT = Error::Candle raised by the device.
+ *  - A model is immutable after creation and may be shared by threads (the reference's
+ *    Stt/Tts are Send + Sync, stt/mod.rs:159). A state is owned by one thread at a time
+ *    (the reference mutates TransformerState through &mut).
+ *  - There is no CPU fallback: without a B200 every call that touches the device fails with
+ *    SVL_ERR_CUDA.
+ */
+#ifndef SVL_CUDA_H
+#define SVL_CUDA_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define SVL_API __attribute__((visibility("default")))
+#else
+#define SVL_API
+#endif
+
+typedef enum svl_status {
+  SVL_OK = 0,
+  SVL_ERR_CONFIG = 1,        /* Error::Config: bad config or weight shapes */
+  SVL_ERR_INVALID_INPUT = 2, /* Error::InvalidInput: token ids, batch, lengths */
+  SVL_ERR_CUDA = 3,          /* a CUDA runtime error (no device, launch failure) */
+  SVL_ERR_OOM = 4,           /* device allocation failed */
+  SVL_ERR_TIMEOUT = 5,       /* a bounded device-side wait expired */
+  SVL_ERR_UNSUPPORTED = 6    /* a config this build does not implement */
+} svl_status;
+
+/* FeedForward (nn/transformer.rs:19-24). */
+typedef enum { SVL_FFN_PLAIN_GELU_TANH = 0, SVL_FFN_PLAIN_GELU_ERF = 1, SVL_FFN_GATED_SILU = 2 } svl_ffn_kind;
+/* Norm (nn/transformer.rs:13-16). */
+typedef enum { SVL_NORM_LAYER = 0, SVL_NORM_RMS = 1 } svl_norm_kind;
+/* Weight storage. Q8_0 is what Linear::from_weight builds (nn/mod.rs:76-88); Q4_1 (32
+ * 4-bit values with an f16 scale and min) has no reference counterpart. */
+typedef enum { SVL_DT_F32 = 0, SVL_DT_BF16 = 1, SVL_DT_Q8_0 = 2, SVL_DT_Q4_1 = 3 } svl_dtype;
+
+/* TransformerConfig (nn/transformer.rs:27-41). `quantize` becomes weight_dtype; context 0
+ * means None (unlimited). kv_dtype is F32 (the reference CPU path) or BF16 (its CUDA path,
+ * stt/mod.rs:193). */
+typedef struct svl_transformer_config {
+  int32_t d_model, num_layers, num_heads, num_kv_heads, head_dim;
+  int32_t ffn_kind;
+  int32_t ffn_hidden;
+  int32_t norm_kind;
+  float norm_eps;
+  int32_t layer_scale;
+  int32_t context;
+  int32_t weight_dtype;
+  int32_t kv_dtype;
+  int32_t _pad;
+  double max_period;
+} svl_transformer_config;
+
+/* The fields of SttConfig (stt/model.rs:17-43) that the language model uses. */
+typedef struct svl_stt_config {
+  int32_t card, n_q, text_card, extra_heads_num, extra_heads_dim, _pad;
+} svl_stt_config;
+
+/* The fields of FlowLmConfig / FlowHeadConfig (tts/config.rs:177-219) the step uses.
+ * flow_kind: 0 lsd, 1 flow_matching, 2 drifting, 3 pointwise (FlowKind, tts/config.rs:177). */
+typedef struct svl_tts_config {
+  int32_t latent_dim, flow_dim, flow_depth, flow_kind, text_bins, _pad;
+} svl_tts_config;
+
+/* One named f32 tensor in host memory, row-major. The names are the reference's safetensors
+ * names (stt/model.rs:224-231, nn/transformer.rs:206-218, :305-312, :429-432,
+ * tts/flow_lm.rs:78-124). */
+typedef struct svl_tensor_view {
+  const char* name;
+  const float* data;
+  int64_t numel;
+} svl_tensor_view;
+
+typedef struct svl_model svl_model;
+typedef struct svl_state svl_state;
+
+/* LanguageModel::new (stt/model.rs:196-233) on `device`: uploads, converts and (for Q8_0 /
+ * Q4_1) quantises the weights like Linear::from_weight (nn/mod.rs:76-88). */
+SVL_API svl_status svl_stt_model_create(const svl_transformer_config* cfg,
+                                        const svl_stt_config* stt,
+                                        const svl_tensor_view* tensors, int32_t n_tensors,
+                                        int32_t device, svl_model** out);
+
+/* FlowLm::new (tts/flow_lm.rs:45-126). */
+SVL_API svl_status svl_tts_model_create(const svl_transformer_config* cfg,
+                                        const svl_tts_config* tts,
+                                        const svl_tensor_view* tensors, int32_t n_tensors,
+                                        int32_t device, svl_model** out);
+
+SVL_API void svl_model_destroy(svl_model* model);
+
+/* Bytes of weights the model streams per step (the roofline numerator without KV). */
+SVL_API int64_t svl_model_weight_bytes(const svl_model* model);
+
+/* Transformer::init_state (nn/transformer.rs:127-136) for up to max_batch independent
+ * streams. Each stream holds a KV ring of `context` slots per layer (or max_positions slots
+ * without a window) and its own position. */
+SVL_API svl_status svl_state_create(svl_model* model, int32_t max_batch, int32_t max_positions,
+                                    svl_state** out);
+SVL_API void svl_state_destroy(svl_state* state);
+/* Back to position 0 (a fresh init_state) for one stream, or all when stream < 0. */
+SVL_API svl_status svl_state_reset(svl_state* state, int32_t stream);
+/* TransformerState position of a stream (nn/transformer.rs:53-56). */
+SVL_API svl_status svl_state_position(svl_state* state, int32_t stream, int32_t* position);
+/* TransformerState::duplicate (nn/transformer.rs:64-73): copy stream src of `from` into
+ * stream dst of `to` (same model). */
+SVL_API svl_status svl_state_copy(svl_state* to, int32_t dst, const svl_state* from, int32_t src);
+/* TransformerState::layer_caches (nn/transformer.rs:76-78): the keys and values a stream can
+ * still attend to, as [kv_heads][len][head_dim] f32 per layer, oldest first. k and v hold
+ * kv_heads * capacity * head_dim floats; *len receives the entry count. */
+SVL_API svl_status svl_state_export(svl_state* state, int32_t stream, int32_t layer, float* k,
+                                    float* v, int32_t* len, int32_t* position);
+/* TransformerState::from_layer_caches (nn/transformer.rs:81-103) for one layer: k and v
+ * [kv_heads][len][head_dim] are the entries of positions position-len .. position-1. Call for
+ * every layer with the same position; from_layer_caches is position == len. Slots of the
+ * window older than the imported entries keep their contents; len == 0 only moves the
+ * stream to `position`. */
+SVL_API svl_status svl_state_import(svl_state* state, int32_t stream, int32_t layer,
+                                    const float* k, const float* v, int32_t len,
+                                    int32_t position);
+
+/* LanguageModel::step (stt/model.rs:239-277) for streams 0..batch-1, host buffers:
+ * text_tokens [batch], audio_tokens [batch][n_q] in, out_tokens [batch] (greedy argmax,
+ * lowest index on ties) out. out_logits [batch][text_card] and out_extra
+ * [batch][extra_heads_num] (softmax p[0] of each extra head) may be NULL. */
+SVL_API svl_status svl_stt_step(svl_model* model, svl_state* state, int32_t batch,
+                                const uint32_t* text_tokens, const uint32_t* audio_tokens,
+                                uint32_t* out_tokens, float* out_logits, float* out_extra);
+
+/* The same step on device buffers, enqueued on `cuda_stream` (a cudaStream_t, NULL = the
+ * model's stream) without host synchronisation. The step is one CUDA graph per batch size. */
+SVL_API svl_status svl_stt_step_device(svl_model* model, svl_state* state, int32_t batch,
+                                       const uint32_t* d_text_tokens,
+                                       const uint32_t* d_audio_tokens, uint32_t* d_out_tokens,
+                                       float* d_out_logits, void* cuda_stream);
+
+/* Recognizer::step's token loop (stt/mod.rs:551-565) for n_frames frames: each stream's
+ * first step (position 0) sees the initial tokens (audio = card, text = text_card), later
+ * steps feed back the previous argmax on the device. audio_tokens [n_frames][batch][n_q],
+ * out_tokens [n_frames][batch], host memory. */
+SVL_API svl_status svl_stt_run_frames(svl_model* model, svl_state* state, int32_t batch,
+                                      int32_t n_frames, const uint32_t* audio_tokens,
+                                      uint32_t* out_tokens);
+
+/* Transformer::forward (nn/transformer.rs:139-154) of one stream over xs [t][d_model] (host,
+ * in place), t >= 1: the prefill path. */
+SVL_API svl_status svl_transformer_forward(svl_model* model, svl_state* state, int32_t stream,
+                                           float* xs, int32_t t);
+
+/* FlowLm::prompt_text (tts/flow_lm.rs:150-158) for one stream. */
+SVL_API svl_status svl_tts_prompt_text(svl_model* model, svl_state* state, int32_t stream,
+                                       const uint32_t* tokens, int32_t n);
+
+/* FlowLm::step (tts/flow_lm.rs:162-185) for streams 0..batch-1: latent_in [batch][latent]
+ * (NULL = BOS for every stream), noise [batch][latent] (the reference samples it on the host,
+ * flow_lm.rs:187-203), latent_out [batch][latent], eos_logit [batch]. */
+SVL_API svl_status svl_tts_step(svl_model* model, svl_state* state, int32_t batch,
+                                const float* latent_in, const float* noise, int32_t decode_steps,
+                                float* latent_out, float* eos_logit);
+
+/* Profiling hook (no counterpart in the reference): enqueues `iters` repetitions of one
+ * kernel family of the STT step for streams 0..batch-1 on `cuda_stream` so a caller can time
+ * it with CUDA events on that stream. which = 0: every weight product of a step (the layer
+ * linears and the head); which = 1: every layer's attention. The repetitions overwrite the
+ * state's activations and KV slots at the current positions, so the state must be reset
+ * before it is used again. *bytes_per_iter receives the algorithmic HBM bytes of one
+ * repetition (weights, or the KV rows read at the current positions). */
+SVL_API svl_status svl_profile_kernels(svl_model* model, svl_state* state, int32_t batch,
+                                       int32_t which, int32_t iters, void* cuda_stream,
+                                       int64_t* bytes_per_iter);
+
+/* Message of the last failure on this thread ("" when none). */
+SVL_API const char* svl_last_error(void);
+SVL_API const char* svl_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

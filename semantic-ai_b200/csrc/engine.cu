@@ -1,0 +1,639 @@
+// engine.cu — weight loading, per-stream state and the step sequence of the LM.
+#include "engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+
+namespace svl {
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return;
+  cudaGetLastError();
+  if (e == cudaErrorMemoryAllocation)
+    throw Error(SVL_ERR_OOM, std::string(what) + ": " + cudaGetErrorString(e));
+  throw Error(SVL_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+DevBuf& DevBuf::operator=(DevBuf&& o) noexcept {
+  if (this != &o) {
+    if (p) cudaFree(p);
+    p = o.p;
+    bytes = o.bytes;
+    o.p = nullptr;
+    o.bytes = 0;
+  }
+  return *this;
+}
+DevBuf::~DevBuf() {
+  if (p) cudaFree(p);
+}
+void DevBuf::alloc(size_t n) {
+  if (p) cudaFree(p);
+  p = nullptr;
+  bytes = 0;
+  if (n == 0) return;
+  check_cuda(cudaMalloc(&p, n), "cudaMalloc");
+  bytes = n;
+}
+HostBuf::~HostBuf() {
+  if (p) cudaFreeHost(p);
+}
+void HostBuf::alloc(size_t n) {
+  if (p) cudaFreeHost(p);
+  p = nullptr;
+  check_cuda(cudaMallocHost(&p, n ? n : 16), "cudaMallocHost");
+  bytes = n;
+}
+
+Model::~Model() {
+  if (stream) cudaStreamDestroy(stream);
+}
+
+State::~State() {
+  for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+}
+
+namespace {
+
+struct Loader {
+  Model& m;
+  const svl_tensor_view* t;
+  int n;
+  DevBuf staging;
+
+  const svl_tensor_view* find(const std::string& name) const {
+    for (int i = 0; i < n; i++)
+      if (t[i].name && name == t[i].name) return &t[i];
+    return nullptr;
+  }
+  const svl_tensor_view& need(const std::string& name, int64_t numel) const {
+    const svl_tensor_view* v = find(name);
+    if (!v) throw Error(SVL_ERR_CONFIG, "missing tensor " + name);
+    if (v->numel != numel)
+      throw Error(SVL_ERR_CONFIG, "tensor " + name + ": " + std::to_string(v->numel) +
+                                      " elements, expected " + std::to_string(numel));
+    if (!v->data) throw Error(SVL_ERR_CONFIG, "tensor " + name + " has no data");
+    return *v;
+  }
+  bool bf16() const { return m.cfg.weight_dtype == SVL_DT_BF16; }
+
+  // f32 vector on the device (rounded to bf16 values when the model runs in bf16, as the
+  // reference's loader converts every tensor to the model dtype).
+  DevBuf vec(const std::string& name, int64_t numel) {
+    const svl_tensor_view& v = need(name, numel);
+    DevBuf b;
+    b.alloc(numel * 4);
+    // Every transfer is ordered on the model's (non-blocking) stream: a plain cudaMemcpy from
+    // pageable memory may return before its DMA lands, unordered with that stream's kernels.
+    check_cuda(cudaMemcpyAsync(b.p, v.data, numel * 4, cudaMemcpyHostToDevice, m.stream), "upload");
+    if (bf16()) launch_round_bf16_inplace(b.as<float>(), numel, m.stream);
+    check_cuda(cudaStreamSynchronize(m.stream), "upload");
+    m.weight_bytes += numel * 4;
+    return b;
+  }
+
+  float* stage(const svl_tensor_view& v) {
+    size_t bytes = v.numel * 4;
+    if (staging.bytes < bytes) {
+      check_cuda(cudaStreamSynchronize(m.stream), "upload");
+      staging.alloc(bytes);
+    }
+    check_cuda(cudaMemcpyAsync(staging.p, v.data, bytes, cudaMemcpyHostToDevice, m.stream), "upload");
+    return staging.as<float>();
+  }
+
+  // Linear::from_weight (nn/mod.rs:76-88): Q8_0 / Q4_1 when requested and k % 32 == 0, else
+  // dense in the model dtype.
+  void linear(Linear& L, const std::string& wname, const std::string& bname, int n_out, int k,
+              bool quantizable, int interleave = 0) {
+    const svl_tensor_view& v = need(wname, (int64_t)n_out * k);
+    if (k % QBLK) throw Error(SVL_ERR_UNSUPPORTED, "linear " + wname + ": k % 32 != 0");
+    int wt = W_F32;
+    switch (m.cfg.weight_dtype) {
+      case SVL_DT_BF16: wt = W_BF16; break;
+      case SVL_DT_Q8_0: wt = quantizable ? W_Q8 : W_F32; break;
+      case SVL_DT_Q4_1: wt = quantizable ? W_Q4 : W_F32; break;
+      default: wt = W_F32;
+    }
+    L.n = n_out;
+    L.k = k;
+    L.wtype = wt;
+    L.interleave = interleave;
+    L.row_stride = packed_row_stride(wt, k);
+    L.w.alloc(L.row_stride * n_out);
+    float* src = stage(v);
+    launch_pack_linear(src, L.w.as<uint8_t>(), L.row_stride, n_out, k, wt, interleave, m.stream);
+    check_cuda(cudaStreamSynchronize(m.stream), "pack weights");
+    if (!bname.empty()) L.bias = vec(bname, n_out);
+    m.weight_bytes += L.row_stride * n_out;
+  }
+
+  void norm(Norm& N, const std::string& prefix, int d) {
+    if (m.cfg.norm_kind == SVL_NORM_RMS) {
+      N.kind = NORM_RMS;
+      N.w = vec(prefix + ".alpha", d);
+    } else {
+      N.kind = NORM_LAYER;
+      N.w = vec(prefix + ".weight", d);
+      N.b = vec(prefix + ".bias", d);
+    }
+    N.eps = m.cfg.norm_eps;
+  }
+
+  void transformer(const std::string& pre) {
+    const auto& c = m.cfg;
+    const int d = c.d_model, qd = c.num_heads * c.head_dim, kvd = c.num_kv_heads * c.head_dim;
+    m.layers.resize(c.num_layers);
+    for (int l = 0; l < c.num_layers; l++) {
+      Layer& L = m.layers[l];
+      const std::string p = pre + "layers." + std::to_string(l) + ".";
+      norm(L.norm1, p + "norm1", d);
+      norm(L.norm2, p + "norm2", d);
+      if (c.layer_scale) {
+        L.ls1 = vec(p + "layer_scale_1.scale", d);
+        L.ls2 = vec(p + "layer_scale_2.scale", d);
+      }
+      // Attention::new (nn/transformer.rs:300-316): in_proj_weight (moshi) or
+      // in_proj.weight (Pocket TTS).
+      std::string inw = p + "self_attn.in_proj_weight";
+      if (!find(inw)) inw = p + "self_attn.in_proj.weight";
+      linear(L.in_proj, inw, "", qd + 2 * kvd, d, true);
+      linear(L.out_proj, p + "self_attn.out_proj.weight", "", d, qd, true);
+      // FeedForwardLayer::new (nn/transformer.rs:418-436).
+      if (c.ffn_kind == SVL_FFN_GATED_SILU) {
+        linear(L.ff1, p + "gating.linear_in.weight", "", 2 * c.ffn_hidden, d, true, c.ffn_hidden);
+        linear(L.ff2, p + "gating.linear_out.weight", "", d, c.ffn_hidden, true);
+      } else {
+        linear(L.ff1, p + "linear1.weight", "", c.ffn_hidden, d, true);
+        linear(L.ff2, p + "linear2.weight", "", d, c.ffn_hidden, true);
+      }
+    }
+    // RoPE inverse frequencies: computed in f64, stored f32 (nn/transformer.rs:114-118).
+    const int half = c.head_dim / 2;
+    std::vector<float> inv(half);
+    for (int i = 0; i < half; i++)
+      inv[i] = (float)std::exp(-std::log(c.max_period) * 2.0 * (double)i / (double)c.head_dim);
+    m.inv_freq.alloc(half * 4);
+    check_cuda(cudaMemcpyAsync(m.inv_freq.p, inv.data(), half * 4, cudaMemcpyHostToDevice, m.stream), "upload");
+    check_cuda(cudaStreamSynchronize(m.stream), "upload");
+  }
+
+  // Embedding tables, f32 (bf16 in a bf16 model).
+  void table(DevBuf& dst, int64_t offset_rows, const std::string& name, int64_t rows, int d) {
+    const svl_tensor_view& v = need(name, rows * d);
+    if (m.tables_bf16) {
+      float* src = stage(v);
+      launch_f32_to_bf16(src, dst.as<uint8_t>() + offset_rows * d * 2, rows * d, m.stream);
+      check_cuda(cudaStreamSynchronize(m.stream), "convert table");
+    } else {
+      check_cuda(cudaMemcpyAsync(dst.as<uint8_t>() + offset_rows * d * 4, v.data, rows * d * 4,
+                                 cudaMemcpyHostToDevice, m.stream),
+                 "upload");
+      check_cuda(cudaStreamSynchronize(m.stream), "upload");
+    }
+  }
+};
+
+void validate_cfg(const svl_transformer_config& c) {
+  auto bad = [](const std::string& m) { throw Error(SVL_ERR_CONFIG, m); };
+  if (c.d_model <= 0 || c.num_layers <= 0 || c.num_heads <= 0 || c.num_kv_heads <= 0 ||
+      c.head_dim <= 0)
+    bad("non-positive transformer dimension");
+  if (c.num_heads % c.num_kv_heads) bad("num_heads must be a multiple of num_kv_heads");
+  if (c.head_dim != 64 && c.head_dim != 128)
+    throw Error(SVL_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (c.d_model % 32) throw Error(SVL_ERR_UNSUPPORTED, "d_model must be a multiple of 32");
+  if (c.ffn_kind < 0 || c.ffn_kind > 2) bad("unknown feed-forward kind");
+  if (c.norm_kind < 0 || c.norm_kind > 1) bad("unknown norm kind");
+  if (c.weight_dtype < 0 || c.weight_dtype > 3) bad("unknown weight dtype");
+  if (c.kv_dtype < 0 || c.kv_dtype > 1) bad("unknown kv dtype");
+  if (c.context < 0) bad("negative context");
+  if (c.ffn_hidden <= 0) bad("non-positive ffn_hidden");
+  if (!(c.max_period > 0)) bad("max_period must be positive");
+}
+
+}  // namespace
+
+Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_config* stt,
+                    const svl_tts_config* tts, const svl_tensor_view* t, int n, int device) {
+  validate_cfg(cfg);
+  int count = 0;
+  check_cuda(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+  if (device < 0 || device >= count) throw Error(SVL_ERR_CUDA, "no such CUDA device");
+  check_cuda(cudaSetDevice(device), "cudaSetDevice");
+  gemv_init_device();
+  Model* m = new Model();
+  try {
+    m->kind = kind;
+    m->device = device;
+    m->cfg = cfg;
+    check_cuda(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "stream");
+    Loader ld{*m, t, n, {}};
+    const int d = cfg.d_model;
+    if (kind == 0) {
+      if (!stt) throw Error(SVL_ERR_CONFIG, "missing STT config");
+      m->stt = *stt;
+      if (stt->n_q < 0 || stt->card <= 0 || stt->text_card <= 0)
+        throw Error(SVL_ERR_CONFIG, "invalid STT config");
+      // LanguageModel::new (stt/model.rs:196-233).
+      m->tables_bf16 = cfg.weight_dtype == SVL_DT_BF16;
+      const int elt = m->tables_bf16 ? 2 : 4;
+      m->text_emb.alloc((int64_t)(stt->text_card + 1) * d * elt);
+      ld.table(m->text_emb, 0, "text_emb.weight", stt->text_card + 1, d);
+      m->audio_emb.alloc((int64_t)std::max(stt->n_q, 1) * (stt->card + 1) * d * elt);
+      for (int c = 0; c < stt->n_q; c++)
+        ld.table(m->audio_emb, (int64_t)c * (stt->card + 1), "emb." + std::to_string(c) + ".weight",
+                 stt->card + 1, d);
+      m->weight_bytes += (int64_t)(1 + stt->n_q) * d * elt;  // rows read per step
+      ld.transformer("transformer.");
+      m->out_norm.kind = NORM_RMS;
+      m->out_norm.eps = 1e-8f;
+      m->out_norm.w = ld.vec("out_norm.alpha", d);
+      ld.linear(m->text_linear, "text_linear.weight", "", stt->text_card, d, true);
+      m->extra.resize(std::max(stt->extra_heads_num, 0));
+      for (int i = 0; i < stt->extra_heads_num; i++)
+        ld.linear(m->extra[i], "extra_heads." + std::to_string(i) + ".weight", "",
+                  stt->extra_heads_dim, d, false);
+    } else {
+      throw Error(SVL_ERR_UNSUPPORTED, "the Pocket-TTS step is not built yet");
+    }
+    check_cuda(cudaStreamSynchronize(m->stream), "load");
+  } catch (...) {
+    delete m;
+    throw;
+  }
+  return m;
+}
+
+State* create_state(Model* m, int max_batch, int max_positions) {
+  if (max_batch <= 0) throw Error(SVL_ERR_INVALID_INPUT, "max_batch must be positive");
+  check_cuda(cudaSetDevice(m->device), "cudaSetDevice");
+  const auto& c = m->cfg;
+  State* s = new State();
+  try {
+    s->m = m;
+    s->max_batch = max_batch;
+    s->windowed = c.context > 0;
+    s->cap = s->windowed ? c.context : max_positions;
+    if (s->cap <= 0) throw Error(SVL_ERR_INVALID_INPUT, "max_positions must be positive without a window");
+    s->kv_elt = c.kv_dtype == SVL_DT_BF16 ? 2 : 4;
+    s->ring_stream_stride = (int64_t)c.num_kv_heads * s->cap * c.head_dim;
+    s->ring_layer_stride = s->ring_stream_stride * max_batch;
+    const int64_t ring_bytes = s->ring_layer_stride * c.num_layers * s->kv_elt;
+    s->k_ring.alloc(ring_bytes);
+    s->v_ring.alloc(ring_bytes);
+    check_cuda(cudaMemsetAsync(s->k_ring.p, 0, ring_bytes, m->stream), "memset");
+    check_cuda(cudaMemsetAsync(s->v_ring.p, 0, ring_bytes, m->stream), "memset");
+    s->pos.alloc(max_batch * 4);
+    check_cuda(cudaMemsetAsync(s->pos.p, 0, max_batch * 4, m->stream), "memset");
+    s->hpos.assign(max_batch, 0);
+    const int d = c.d_model, qd = c.num_heads * c.head_dim;
+    s->x.alloc((int64_t)max_batch * d * 4);
+    s->q.alloc((int64_t)max_batch * qd * 4);
+    s->attn.alloc((int64_t)max_batch * qd * 4);
+    s->act.alloc((int64_t)max_batch * c.ffn_hidden * 4);
+    // Split the keys of a (stream, head) so that batch 1 still covers the SMs.
+    const int units = max_batch * c.num_heads;
+    int splits = (2 * 148 + units - 1) / units;
+    splits = std::max(1, std::min(splits, (s->cap + 31) / 32));
+    s->splits = splits;
+    s->part.alloc((int64_t)max_batch * c.num_heads * splits * (c.head_dim + 2) * 4);
+    s->tickets.alloc((int64_t)max_batch * c.num_heads * 4);
+    check_cuda(cudaMemsetAsync(s->tickets.p, 0, s->tickets.bytes, m->stream), "memset");
+    s->am_val.alloc(kMaxNbChunk * kLogitsGrid * 4);
+    s->am_idx.alloc(kMaxNbChunk * kLogitsGrid * 4);
+    s->am_ticket.alloc(4);
+    check_cuda(cudaMemsetAsync(s->am_ticket.p, 0, 4, m->stream), "memset");
+    s->err.alloc(4);
+    check_cuda(cudaMemsetAsync(s->err.p, 0, 4, m->stream), "memset");
+    if (m->kind == 0) {
+      const auto& st = m->stt;
+      s->logits.alloc((int64_t)max_batch * st.text_card * 4);
+      s->tok_in.alloc(max_batch * 4);
+      s->tok_out.alloc(max_batch * 4);
+      s->audio_in.alloc((int64_t)max_batch * std::max(st.n_q, 1) * 4);
+      if (st.extra_heads_num > 0) {
+        s->extra_logits.alloc((int64_t)max_batch * st.extra_heads_num * st.extra_heads_dim * 4);
+        s->extra_p.alloc((int64_t)max_batch * st.extra_heads_num * 4);
+      }
+      s->h_tok_in.alloc(max_batch * 4);
+      s->h_tok_out.alloc(max_batch * 4);
+      s->h_audio_in.alloc((int64_t)max_batch * std::max(st.n_q, 1) * 4);
+    }
+    // tok_out holds each stream's last argmax (the text token a resumed stream feeds back).
+    if (m->kind == 0) check_cuda(cudaMemsetAsync(s->tok_out.p, 0, max_batch * 4, m->stream), "memset");
+    check_cuda(cudaStreamSynchronize(m->stream), "state init");
+  } catch (...) {
+    delete s;
+    throw;
+  }
+  return s;
+}
+
+namespace {
+
+GemvParams gemv_base(const Linear& L, const float* x, int64_t x_stride, int nb) {
+  GemvParams p{};
+  p.w = L.w.as<uint8_t>();
+  p.row_stride = L.row_stride;
+  p.n = L.n;
+  p.k = L.k;
+  p.wtype = L.wtype;
+  p.x = x;
+  p.x_stride = x_stride;
+  p.nb = nb;
+  p.norm = NORM_NONE;
+  p.bias = L.bias.as<float>();
+  return p;
+}
+
+void set_norm(GemvParams& p, const Norm& N) {
+  p.norm = N.kind;
+  p.norm_w = N.w.as<float>();
+  p.norm_b = N.b.as<float>();
+  p.eps = N.eps;
+}
+
+}  // namespace
+
+void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bool do_lin,
+                         bool do_attn);
+
+void enqueue_layers(Model& m, State& s, int b0, int nb, cudaStream_t st) {
+  enqueue_layers_mask(m, s, b0, nb, st, true, true);
+}
+
+void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bool do_lin,
+                         bool do_attn) {
+  const auto& c = m.cfg;
+  const int d = c.d_model, hd = c.head_dim, qd = c.num_heads * hd, kvd = c.num_kv_heads * hd;
+  float* x = s.x.as<float>() + (int64_t)b0 * d;
+  float* q = s.q.as<float>() + (int64_t)b0 * qd;
+  float* attn = s.attn.as<float>() + (int64_t)b0 * qd;
+  float* act = s.act.as<float>() + (int64_t)b0 * c.ffn_hidden;
+  const int* pos = s.pos.as<int>() + b0;
+  for (int l = 0; l < c.num_layers; l++) {
+    const Layer& L = m.layers[l];
+    uint8_t* kr = s.k_ring.as<uint8_t>() + ((int64_t)l * s.ring_layer_stride + (int64_t)b0 * s.ring_stream_stride) * s.kv_elt;
+    uint8_t* vr = s.v_ring.as<uint8_t>() + ((int64_t)l * s.ring_layer_stride + (int64_t)b0 * s.ring_stream_stride) * s.kv_elt;
+    // norm1 + in_proj + RoPE + KV-ring write (nn/transformer.rs:329-342).
+    GemvParams g = gemv_base(L.in_proj, x, d, nb);
+    set_norm(g, L.norm1);
+    g.epi = EPI_QKV_ROPE;
+    g.out = q;
+    g.out_stride = qd;
+    g.inv_freq = m.inv_freq.as<float>();
+    g.pos = pos;
+    g.q_dim = qd;
+    g.kv_dim = kvd;
+    g.head_dim = hd;
+    g.ring_cap = s.cap;
+    g.windowed = s.windowed;
+    g.k_ring = kr;
+    g.v_ring = vr;
+    g.ring_stream_stride = s.ring_stream_stride;
+    g.kv_bf16 = s.kv_elt == 2;
+    if (do_lin) launch_gemv(g, st);
+    // Sliding-window attention (nn/kernels/attention.rs:81-169).
+    AttnParams a{};
+    a.q = q;
+    a.k_ring = kr;
+    a.v_ring = vr;
+    a.ring_stream_stride = s.ring_stream_stride;
+    a.kv_bf16 = s.kv_elt == 2;
+    a.pos = pos;
+    a.nb = nb;
+    a.heads = c.num_heads;
+    a.kv_heads = c.num_kv_heads;
+    a.head_dim = hd;
+    a.ring_cap = s.cap;
+    a.window = c.context;
+    a.scale = std::pow((float)hd, -0.5f);
+    a.splits = s.splits;
+    a.part = s.part.as<float>();
+    a.tickets = s.tickets.as<unsigned>();
+    a.out = attn;
+    if (do_attn) launch_attention_decode(a, st);
+    if (!do_lin) continue;
+    // out_proj + residual (nn/transformer.rs:344, :239-243).
+    g = gemv_base(L.out_proj, attn, qd, nb);
+    g.epi = EPI_RESIDUAL;
+    g.out = x;
+    g.out_stride = d;
+    g.ls = L.ls1.as<float>();
+    launch_gemv(g, st);
+    // norm2 + feed-forward (nn/transformer.rs:438-464).
+    g = gemv_base(L.ff1, x, d, nb);
+    set_norm(g, L.norm2);
+    g.out = act;
+    g.out_stride = c.ffn_hidden;
+    g.epi = c.ffn_kind == SVL_FFN_GATED_SILU ? EPI_SWIGLU
+            : c.ffn_kind == SVL_FFN_PLAIN_GELU_ERF ? EPI_GELU_ERF : EPI_GELU_TANH;
+    launch_gemv(g, st);
+    g = gemv_base(L.ff2, act, c.ffn_hidden, nb);
+    g.epi = EPI_RESIDUAL;
+    g.out = x;
+    g.out_stride = d;
+    g.ls = L.ls2.as<float>();
+    launch_gemv(g, st);
+  }
+}
+
+void launch_extra_heads(const float* logits, int nb, int heads, int dim, float* out,
+                        cudaStream_t st);
+
+void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
+  const auto& c = m.cfg;
+  const int d = c.d_model;
+  EmbedParams e{};
+  e.text_table = m.text_emb.p;
+  e.audio_tables = m.audio_emb.p;
+  e.tables_bf16 = m.tables_bf16;
+  e.text_tok = s.tok_in.as<uint32_t>();
+  e.audio_tok = s.audio_in.as<uint32_t>();
+  e.nb = nb;
+  e.d = d;
+  e.n_q = m.stt.n_q;
+  e.card = m.stt.card;
+  e.text_card = m.stt.text_card;
+  e.x = s.x.as<float>();
+  e.error_flag = s.err.as<int>();
+  launch_embed(e, st);
+  enqueue_layers(m, s, 0, nb, st);
+  // out_norm + text_linear + argmax (stt/model.rs:252-258).
+  GemvParams g = gemv_base(m.text_linear, s.x.as<float>(), d, nb);
+  set_norm(g, m.out_norm);
+  g.epi = EPI_LOGITS;
+  g.out = s.logits.as<float>();
+  g.out_stride = m.stt.text_card;
+  g.am_val = s.am_val.as<float>();
+  g.am_idx = s.am_idx.as<int>();
+  g.am_ticket = s.am_ticket.as<unsigned>();
+  g.tokens = s.tok_out.as<uint32_t>();
+  launch_gemv(g, st);
+  // Extra (VAD) heads: softmax p[0] of each (stt/model.rs:259-271).
+  const int eh = m.stt.extra_heads_num, edim = m.stt.extra_heads_dim;
+  for (int i = 0; i < eh; i++) {
+    GemvParams h = gemv_base(m.extra[i], s.x.as<float>(), d, nb);
+    set_norm(h, m.out_norm);
+    h.epi = EPI_STORE;
+    h.out = s.extra_logits.as<float>() + i * edim;
+    h.out_stride = (int64_t)eh * edim;
+    launch_gemv(h, st);
+  }
+  if (eh > 0) launch_extra_heads(s.extra_logits.as<float>(), nb, eh, edim, s.extra_p.as<float>(), st);
+  launch_advance_positions(s.pos.as<int>(), nb, st);
+}
+
+void launch_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
+  auto it = s.graphs.find(nb);
+  if (it == s.graphs.end()) {
+    cudaGraph_t graph = nullptr;
+    check_cuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      enqueue_stt_step(m, s, nb, st);
+    } catch (...) {
+      cudaStreamEndCapture(st, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    check_cuda(cudaStreamEndCapture(st, &graph), "end capture");
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    check_cuda(e, "graph instantiate");
+    it = s.graphs.emplace(nb, exec).first;
+  }
+  check_cuda(cudaGraphLaunch(it->second, st), "graph launch");
+}
+
+int64_t enqueue_profile(Model& m, State& s, int nb, int which, cudaStream_t st) {
+  const auto& c = m.cfg;
+  if (which == 0) {
+    enqueue_layers_mask(m, s, 0, nb, st, true, false);
+    GemvParams g = gemv_base(m.text_linear, s.x.as<float>(), c.d_model, nb);
+    set_norm(g, m.out_norm);
+    g.epi = EPI_LOGITS;
+    g.out = s.logits.as<float>();
+    g.out_stride = m.text_linear.n;
+    g.am_val = s.am_val.as<float>();
+    g.am_idx = s.am_idx.as<int>();
+    g.am_ticket = s.am_ticket.as<unsigned>();
+    g.tokens = s.tok_out.as<uint32_t>();
+    launch_gemv(g, st);
+    int64_t bytes = m.text_linear.bytes();
+    for (const Layer& L : m.layers)
+      bytes += L.in_proj.bytes() + L.out_proj.bytes() + L.ff1.bytes() + L.ff2.bytes();
+    return bytes;
+  }
+  enqueue_layers_mask(m, s, 0, nb, st, false, true);
+  int64_t bytes = 0;
+  for (int b = 0; b < nb; b++) {
+    const int fill = c.context > 0 ? std::min(s.hpos[b] + 1, c.context) : s.hpos[b] + 1;
+    bytes += (int64_t)c.num_layers * 2 * fill * c.num_kv_heads * c.head_dim * s.kv_elt;
+  }
+  return bytes;
+}
+
+void state_reset(State& s, int stream) {
+  const int b0 = stream < 0 ? 0 : stream, b1 = stream < 0 ? s.max_batch : stream + 1;
+  // State operations wait for every stream (a step may be in flight on a caller's stream),
+  // then transfer in order on the model's stream.
+  check_cuda(cudaDeviceSynchronize(), "reset");
+  for (int b = b0; b < b1; b++) s.hpos[b] = 0;
+  check_cuda(cudaMemcpyAsync(s.pos.as<int>() + b0, s.hpos.data() + b0, (b1 - b0) * 4,
+                             cudaMemcpyHostToDevice, s.m->stream),
+             "reset");
+  check_cuda(cudaStreamSynchronize(s.m->stream), "reset");
+}
+
+void state_export(State& s, int stream, int layer, float* k, float* v, int* len) {
+  const auto& c = s.m->cfg;
+  const int pos = s.hpos[stream];
+  const int n = s.windowed ? std::min(pos, s.cap) : pos;
+  const int64_t elems = s.ring_stream_stride;
+  std::vector<uint8_t> hk(elems * s.kv_elt), hv(elems * s.kv_elt);
+  const int64_t off = ((int64_t)layer * s.ring_layer_stride + (int64_t)stream * s.ring_stream_stride) * s.kv_elt;
+  check_cuda(cudaDeviceSynchronize(), "export");
+  check_cuda(cudaMemcpyAsync(hk.data(), s.k_ring.as<uint8_t>() + off, hk.size(), cudaMemcpyDeviceToHost, s.m->stream), "export");
+  check_cuda(cudaMemcpyAsync(hv.data(), s.v_ring.as<uint8_t>() + off, hv.size(), cudaMemcpyDeviceToHost, s.m->stream), "export");
+  check_cuda(cudaStreamSynchronize(s.m->stream), "export");
+  auto get = [&](const std::vector<uint8_t>& src, int64_t i) -> float {
+    if (s.kv_elt == 4) {
+      float f;
+      std::memcpy(&f, src.data() + i * 4, 4);
+      return f;
+    }
+    uint16_t h;
+    std::memcpy(&h, src.data() + i * 2, 2);
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+  };
+  const int hd = c.head_dim;
+  for (int h = 0; h < c.num_kv_heads; h++)
+    for (int j = 0; j < n; j++) {
+      const int p = pos - n + j;
+      const int slot = s.windowed ? p % s.cap : p;
+      for (int i = 0; i < hd; i++) {
+        const int64_t src = ((int64_t)h * s.cap + slot) * hd + i;
+        const int64_t dst = ((int64_t)h * n + j) * hd + i;
+        k[dst] = get(hk, src);
+        v[dst] = get(hv, src);
+      }
+    }
+  *len = n;
+}
+
+void state_import(State& s, int stream, int layer, const float* k, const float* v, int len,
+                  int position) {
+  const auto& c = s.m->cfg;
+  if (len < 0 || position < len) throw Error(SVL_ERR_INVALID_INPUT, "import: need 0 <= len <= position");
+  if (!s.windowed && position > s.cap)
+    throw Error(SVL_ERR_INVALID_INPUT, "import: position exceeds the state's max_positions");
+  check_cuda(cudaDeviceSynchronize(), "import");
+  if (len == 0) {
+    // Only the position moves; the ring keeps its contents.
+    s.hpos[stream] = position;
+    check_cuda(cudaMemcpyAsync(s.pos.as<int>() + stream, &position, 4, cudaMemcpyHostToDevice, s.m->stream), "import");
+    check_cuda(cudaStreamSynchronize(s.m->stream), "import");
+    return;
+  }
+  const int keep = s.windowed ? std::min(len, s.cap) : len;
+  const int hd = c.head_dim;
+  const int64_t elems = s.ring_stream_stride;
+  std::vector<uint8_t> hk(elems * s.kv_elt, 0), hv(elems * s.kv_elt, 0);
+  auto put = [&](std::vector<uint8_t>& dst, int64_t i, float f) {
+    if (s.kv_elt == 4) {
+      std::memcpy(dst.data() + i * 4, &f, 4);
+    } else {
+      uint32_t u;
+      std::memcpy(&u, &f, 4);
+      u += 0x7fffu + ((u >> 16) & 1u);
+      uint16_t h = (uint16_t)(u >> 16);
+      std::memcpy(dst.data() + i * 2, &h, 2);
+    }
+  };
+  for (int h = 0; h < c.num_kv_heads; h++)
+    for (int j = len - keep; j < len; j++) {
+      const int p = position - len + j;
+      const int slot = s.windowed ? p % s.cap : p;
+      for (int i = 0; i < hd; i++) {
+        const int64_t src = ((int64_t)h * len + j) * hd + i;
+        const int64_t dst = ((int64_t)h * s.cap + slot) * hd + i;
+        put(hk, dst, k[src]);
+        put(hv, dst, v[src]);
+      }
+    }
+  const int64_t off = ((int64_t)layer * s.ring_layer_stride + (int64_t)stream * s.ring_stream_stride) * s.kv_elt;
+  check_cuda(cudaMemcpyAsync(s.k_ring.as<uint8_t>() + off, hk.data(), hk.size(), cudaMemcpyHostToDevice, s.m->stream), "import");
+  check_cuda(cudaMemcpyAsync(s.v_ring.as<uint8_t>() + off, hv.data(), hv.size(), cudaMemcpyHostToDevice, s.m->stream), "import");
+  s.hpos[stream] = position;
+  check_cuda(cudaMemcpyAsync(s.pos.as<int>() + stream, &position, 4, cudaMemcpyHostToDevice, s.m->stream), "import");
+  check_cuda(cudaStreamSynchronize(s.m->stream), "import");
+}
+
+}  // namespace svl

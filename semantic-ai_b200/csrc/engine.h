@@ -1,0 +1,155 @@
+// engine.h — host side of the B200 streaming LM step: weights on the device, per-stream KV
+// rings, and the step as a sequence of kernels captured once per batch size in a CUDA
+// graph. Mirrors the reference's types: Transformer / TransformerState
+// (nn/transformer.rs:43-104), LanguageModel (stt/model.rs:176-186) and FlowLm
+// (tts/flow_lm.rs:24-42).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/svl_cuda.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace svl {
+
+// An error carrying the C-ABI status it maps to.
+struct Error : std::runtime_error {
+  svl_status code;
+  Error(svl_status c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+void check_cuda(cudaError_t e, const char* what);
+
+// Owning device allocation.
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; o.bytes = 0; }
+  DevBuf& operator=(DevBuf&& o) noexcept;
+  ~DevBuf();
+  void alloc(size_t n);
+  template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+// Owning pinned host allocation (staging for the host-buffer entry points).
+struct HostBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  HostBuf() = default;
+  HostBuf(const HostBuf&) = delete;
+  HostBuf& operator=(const HostBuf&) = delete;
+  ~HostBuf();
+  void alloc(size_t n);
+  template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+struct Linear {
+  int n = 0, k = 0, wtype = W_F32;
+  int64_t row_stride = 0;
+  int interleave = 0;
+  DevBuf w;
+  DevBuf bias;  // f32 [n] or empty
+  int64_t bytes() const { return row_stride * n + (bias.p ? 4LL * n : 0); }
+};
+
+struct Norm {
+  int kind = NORM_NONE;
+  float eps = 0.f;
+  DevBuf w, b;
+};
+
+struct Layer {
+  Norm norm1, norm2;
+  Linear in_proj, out_proj, ff1, ff2;
+  DevBuf ls1, ls2;
+};
+
+struct TimeEmbed {
+  DevBuf freqs;  // [128]
+  Linear l1, l2;
+  DevBuf alpha;
+};
+
+struct ResBlock {
+  Norm ln;
+  Linear mlp1, mlp2, mod;
+};
+
+struct Model {
+  int kind = 0;  // 0 STT LanguageModel, 1 Pocket-TTS FlowLm
+  int device = 0;
+  svl_transformer_config cfg{};
+  svl_stt_config stt{};
+  svl_tts_config tts{};
+  std::vector<Layer> layers;
+  DevBuf inv_freq;
+  // STT
+  DevBuf text_emb, audio_emb;
+  int tables_bf16 = 0;
+  Norm out_norm;
+  Linear text_linear;
+  std::vector<Linear> extra;
+  // TTS
+  DevBuf cond_table;
+  Linear input_linear, out_eos;
+  DevBuf bos;
+  std::vector<TimeEmbed> time_emb;
+  Linear cond_embed, input_proj, final_mod, final_linear;
+  std::vector<ResBlock> res;
+  int64_t weight_bytes = 0;
+  cudaStream_t stream = nullptr;
+  ~Model();
+};
+
+struct State {
+  Model* m = nullptr;
+  int max_batch = 0, cap = 0, windowed = 0;
+  int kv_elt = 4;
+  int64_t ring_stream_stride = 0;  // elements per stream per layer
+  int64_t ring_layer_stride = 0;   // elements per layer
+  DevBuf k_ring, v_ring;
+  DevBuf pos;
+  std::vector<int> hpos;
+  // work buffers
+  DevBuf x, q, attn, act, logits, extra_logits, extra_p;
+  DevBuf tok_in, audio_in, tok_out;
+  DevBuf am_val, am_idx, am_ticket, part, tickets, err;
+  DevBuf frames_audio, frames_out;  // svl_stt_run_frames
+  // TTS work buffers
+  DevBuf latent_in, noise, latent_out, eos, z, y, sy, hbuf, h2buf, modbuf, xs2, tmp;
+  HostBuf h_tok_in, h_audio_in, h_tok_out;
+  int splits = 1;
+  std::map<int, cudaGraphExec_t> graphs;
+  ~State();
+};
+
+// Weight loading (LanguageModel::new / FlowLm::new).
+Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_config* stt,
+                    const svl_tts_config* tts, const svl_tensor_view* t, int n, int device);
+State* create_state(Model* m, int max_batch, int max_positions);
+
+// The step kernels for streams [b0, b0 + nb) (no embedding / head).
+void enqueue_layers(Model& m, State& s, int b0, int nb, cudaStream_t st);
+// The whole STT step for streams [0, nb): embed tok_in/audio_in, layers, head into tok_out.
+void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st);
+// Runs the captured graph of the STT step for nb streams (captures it on first use).
+void launch_stt_graph(Model& m, State& s, int nb, cudaStream_t st);
+// Profiling: one repetition of the step's weight products (which 0) or attention (which 1).
+int64_t enqueue_profile(Model& m, State& s, int nb, int which, cudaStream_t st);
+void enqueue_tts_step(Model& m, State& s, int nb, int decode_steps, bool bos, cudaStream_t st);
+
+void state_reset(State& s, int stream);
+void state_export(State& s, int stream, int layer, float* k, float* v, int* len);
+void state_import(State& s, int stream, int layer, const float* k, const float* v, int len,
+                  int position);
+
+}  // namespace svl

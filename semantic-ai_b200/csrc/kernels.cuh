@@ -1,0 +1,104 @@
+// kernels.cuh — parameter blocks and launchers of the step kernels (host/device shared).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace svl {
+
+// CTAs of a logits product: the argmax scratch holds one (value, index) pair per CTA.
+constexpr int kLogitsGrid = 148;
+// Streams one product launch covers at most (the argmax scratch is [kMaxNbChunk][kLogitsGrid]).
+constexpr int kMaxNbChunk = 8;
+
+enum GemvEpilogue {
+  EPI_STORE = 0,     // out = acc (+ bias)
+  EPI_RESIDUAL = 1,  // out += (acc (+ bias)) * layer_scale
+  EPI_QKV_ROPE = 2,  // RoPE on q,k; q to a buffer, k and v into the KV ring
+  EPI_SWIGLU = 3,    // rows interleaved gate/value: out[i] = silu(gate) * value
+  EPI_GELU_TANH = 4, // out = gelu_tanh(acc (+ bias))
+  EPI_GELU_ERF = 5,
+  EPI_LOGITS = 6,    // out = acc (+ bias), plus greedy argmax into tokens
+  EPI_SILU = 7       // out = silu(acc (+ bias))
+};
+
+// One matrix-vector product over `nb` streams: out[b] = epilogue(W · norm(x[b])).
+struct GemvParams {
+  const uint8_t* w;      // device weights in the packed layout of `wtype`
+  int64_t row_stride;    // bytes between rows
+  int n, k;              // rows (outputs) and columns (inputs)
+  int wtype;             // WeightType
+  const float* x;        // [nb][x_stride] f32 inputs
+  int64_t x_stride;
+  int nb;
+  int norm;              // NormKind applied to x first
+  const float* norm_w;
+  const float* norm_b;
+  float eps;
+  const float* bias;     // [n] or null
+  int epi;
+  float* out;            // [nb][out_stride]
+  int64_t out_stride;
+  const float* ls;       // layer scale [n] or null (EPI_RESIDUAL)
+  // EPI_QKV_ROPE
+  const float* inv_freq; // [head_dim / 2]
+  const int* pos;        // [nb] absolute positions of the new token
+  int q_dim, kv_dim, head_dim;
+  int ring_cap;          // KV slots per stream and head
+  int windowed;          // slot = pos % ring_cap when set, else pos
+  void* k_ring;          // [nb][kv_heads][ring_cap][head_dim], f32 or bf16
+  void* v_ring;
+  int64_t ring_stream_stride;  // elements between streams
+  int kv_bf16;
+  // EPI_LOGITS
+  float* am_val;         // [nb][grid] scratch
+  int* am_idx;           // [nb][grid] scratch
+  unsigned* am_ticket;   // one counter, zero between launches
+  uint32_t* tokens;      // [nb] argmax out
+};
+
+void launch_gemv(const GemvParams& p, cudaStream_t s);
+// Per device, once: raises the dynamic shared-memory limit of every product kernel.
+void gemv_init_device();
+
+struct AttnParams {
+  const float* q;        // [nb][heads][head_dim] (after RoPE)
+  const void* k_ring;    // [nb][kv_heads][ring_cap][head_dim]
+  const void* v_ring;
+  int64_t ring_stream_stride;
+  int kv_bf16;
+  const int* pos;        // [nb] position of the newest key (already written)
+  int nb, heads, kv_heads, head_dim, ring_cap, window;  // window 0 = unlimited
+  float scale;
+  int splits;            // key chunks per (stream, head)
+  float* part;           // [nb][heads][splits][head_dim + 2] scratch
+  unsigned* tickets;     // [nb][heads], zero between launches
+  float* out;            // [nb][heads * head_dim]
+};
+
+void launch_attention_decode(const AttnParams& p, cudaStream_t s);
+
+struct EmbedParams {
+  const void* text_table;   // [text_card + 1][d]
+  const void* audio_tables; // [n_q][card + 1][d]
+  int tables_bf16;
+  const uint32_t* text_tok; // [nb]
+  const uint32_t* audio_tok;// [nb][n_q]
+  int nb, d, n_q, card, text_card;
+  float* x;                 // [nb][d]
+  int* error_flag;          // set to 1 on an out-of-range id
+};
+
+void launch_embed(const EmbedParams& p, cudaStream_t s);
+void launch_advance_positions(int* pos, int nb, cudaStream_t s);
+
+// Weight packing: f32 [n][k] (device) into the layout of wtype. interleave_half = F swaps
+// rows so that packed row 2i is source row i and 2i+1 is source row F + i (SwiGLU).
+void launch_pack_linear(const float* src, uint8_t* dst, int64_t row_stride, int n, int k,
+                        int wtype, int interleave_half, cudaStream_t s);
+void launch_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t s);
+void launch_round_bf16_inplace(float* p, int64_t n, cudaStream_t s);
+
+int64_t packed_row_stride(int wtype, int k);
+
+}  // namespace svl

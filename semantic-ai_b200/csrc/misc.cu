@@ -1,0 +1,174 @@
+// misc.cu — embedding sum, position advance and weight packing.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace svl {
+namespace {
+
+// LanguageModel::step's input (stt/model.rs:246-250): the text embedding row, then each of
+// the n_q audio embedding rows added in codebook order, in f32. Same order and rounding as
+// the reference, so the sum is bit-identical to it.
+template <bool BF16>
+__global__ void embed_kernel(const EmbedParams p) {
+  const int b = blockIdx.y;
+  const int c4 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c4 * 4 >= p.d) return;
+  uint32_t tt = p.text_tok[b];
+  if (tt > (uint32_t)p.text_card) {
+    atomicExch(p.error_flag, 1);
+    tt = 0;
+  }
+  auto row = [&](const void* table, int64_t r) -> float4 {
+    if (BF16) {
+      const uint2 v = reinterpret_cast<const uint2*>(
+          reinterpret_cast<const __nv_bfloat16*>(table) + r * p.d)[c4];
+      return make_float4(bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y));
+    }
+    return reinterpret_cast<const float4*>(reinterpret_cast<const float*>(table) + r * p.d)[c4];
+  };
+  float4 acc = row(p.text_table, tt);
+  for (int c = 0; c < p.n_q; c++) {
+    uint32_t a = p.audio_tok[b * p.n_q + c];
+    if (a > (uint32_t)p.card) {
+      atomicExch(p.error_flag, 1);
+      a = 0;
+    }
+    float4 e = row(p.audio_tables, (int64_t)c * (p.card + 1) + a);
+    acc.x = acc.x + e.x;
+    acc.y = acc.y + e.y;
+    acc.z = acc.z + e.z;
+    acc.w = acc.w + e.w;
+  }
+  reinterpret_cast<float4*>(p.x + (int64_t)b * p.d)[c4] = acc;
+}
+
+__global__ void advance_kernel(int* pos, int nb) {
+  int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < nb) pos[b] += 1;
+}
+
+// One warp per (packed row, 32-column block).
+__global__ void pack_kernel(const float* src, uint8_t* dst, int64_t row_stride, int n, int k,
+                            int wtype, int interleave_half) {
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nblk = k / QBLK;
+  if (gw >= (int64_t)n * nblk) return;
+  const int r = (int)(gw / nblk), blk = (int)(gw % nblk);
+  int sr = r;
+  if (interleave_half > 0) sr = (r & 1) ? interleave_half + (r >> 1) : (r >> 1);
+  const float x = src[(int64_t)sr * k + blk * QBLK + lane];
+  uint8_t* row = dst + (int64_t)r * row_stride;
+  if (wtype == W_F32) {
+    reinterpret_cast<float*>(row)[blk * QBLK + lane] = x;
+  } else if (wtype == W_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(row)[blk * QBLK + lane] = __float2bfloat16_rn(x);
+  } else if (wtype == W_Q8) {
+    // Q8_0 (ggml; candle QTensor::quantize, nn/mod.rs:81-83): d = amax / 127 stored f16,
+    // q = round(x * (1 / d)).
+    float amax = warp_max(fabsf(x));
+    float d = amax / 127.0f;
+    float id = d != 0.0f ? 1.0f / d : 0.0f;
+    reinterpret_cast<int8_t*>(row)[blk * QBLK + lane] = (int8_t)(int)roundf(x * id);
+    if (lane == 0) reinterpret_cast<__half*>(row + k)[blk] = __float2half_rn(d);
+  } else {
+    // Q4_1 (ggml): d = (max - min) / 15, m = min, q = min(15, trunc((x - min) / d + 0.5)),
+    // byte j holds q[j] (low nibble) and q[j + 16] (high nibble).
+    float mn = x, mx = x;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    float d = (mx - mn) / 15.0f;
+    float id = d != 0.0f ? 1.0f / d : 0.0f;
+    int q = (int)((x - mn) * id + 0.5f);
+    q = q > 15 ? 15 : q;
+    int hi = __shfl_down_sync(0xffffffffu, q, 16);
+    if (lane < 16) row[blk * 16 + lane] = (uint8_t)(q | (hi << 4));
+    if (lane == 0)
+      reinterpret_cast<__half2*>(row + k / 2)[blk] = __halves2half2(__float2half_rn(d), __float2half_rn(mn));
+  }
+}
+
+__global__ void f32_to_bf16_kernel(const float* src, __nv_bfloat16* dst, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+__global__ void round_bf16_kernel(float* p, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = round_bf16(p[i]);
+}
+
+}  // namespace
+
+void launch_embed(const EmbedParams& p, cudaStream_t s) {
+  dim3 grid((p.d / 4 + 127) / 128, p.nb);
+  if (p.tables_bf16)
+    embed_kernel<true><<<grid, 128, 0, s>>>(p);
+  else
+    embed_kernel<false><<<grid, 128, 0, s>>>(p);
+}
+
+void launch_advance_positions(int* pos, int nb, cudaStream_t s) {
+  advance_kernel<<<(nb + 255) / 256, 256, 0, s>>>(pos, nb);
+}
+
+int64_t packed_row_stride(int wtype, int k) {
+  auto pad16 = [](int64_t x) { return (x + 15) / 16 * 16; };
+  switch (wtype) {
+    case W_F32: return pad16((int64_t)k * 4);
+    case W_BF16: return pad16((int64_t)k * 2);
+    case W_Q8: return k + pad16((int64_t)(k / QBLK) * 2);
+    default: return k / 2 + pad16((int64_t)(k / QBLK) * 4);
+  }
+}
+
+void launch_pack_linear(const float* src, uint8_t* dst, int64_t row_stride, int n, int k,
+                        int wtype, int interleave_half, cudaStream_t s) {
+  int64_t warps = (int64_t)n * (k / QBLK);
+  int64_t blocks = (warps * 32 + 255) / 256;
+  pack_kernel<<<(unsigned)blocks, 256, 0, s>>>(src, dst, row_stride, n, k, wtype, interleave_half);
+}
+
+void launch_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t s) {
+  f32_to_bf16_kernel<<<1184, 256, 0, s>>>(src, reinterpret_cast<__nv_bfloat16*>(dst), n);
+}
+
+void launch_round_bf16_inplace(float* p, int64_t n, cudaStream_t s) {
+  round_bf16_kernel<<<1184, 256, 0, s>>>(p, n);
+}
+
+}  // namespace svl
+
+namespace svl {
+namespace {
+
+// softmax_last_dim(head logits)[0] per (stream, extra head) (stt/model.rs:259-271).
+__global__ void extra_p0_kernel(const float* logits, int nb, int heads, int dim, float* out) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nb * heads) return;
+  const float* x = logits + (int64_t)i * dim;
+  float mx = x[0];
+  for (int j = 1; j < dim; j++) mx = fmaxf(mx, x[j]);
+  float sum = 0.f, e0 = 0.f;
+  for (int j = 0; j < dim; j++) {
+    float e = expf(x[j] - mx);
+    if (j == 0) e0 = e;
+    sum = sum + e;
+  }
+  out[i] = e0 / sum;
+}
+
+}  // namespace
+
+void launch_extra_heads(const float* logits, int nb, int heads, int dim, float* out,
+                        cudaStream_t st) {
+  int n = nb * heads;
+  extra_p0_kernel<<<(n + 127) / 128, 128, 0, st>>>(logits, nb, heads, dim, out);
+}
+
+}  // namespace svl
