@@ -14,6 +14,7 @@ namespace svl {
 namespace {
 
 constexpr int kAttnWarps = 4;
+constexpr int kMaxSplits = kAttnWarps * 32;
 
 template <bool BF16>
 __device__ __forceinline__ void load16(const void* base, int64_t off, float* out) {
@@ -61,6 +62,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
 
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // q and the newest key come from the previous kernel (programmatic dependent launch).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int kk = lane / LPK, sub = lane % LPK;
   const int pos = p.pos[b];
   const int count = p.window > 0 ? min(pos + 1, p.window) : pos + 1;
@@ -142,47 +146,77 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
       if (t < HD) A = A + sm_a[w][t] * c;
     }
   const int64_t bh = (int64_t)b * p.heads + h;
+  __shared__ float so[HD];
   if (p.splits == 1) {
-    if (t < HD) p.out[bh * HD + t] = L > 0.f ? A / L : 0.f;
-    return;
+    if (t < HD) so[t] = L > 0.f ? A / L : 0.f;
+  } else {
+    float* part = p.part + (bh * p.splits + split) * (HD + 2);
+    if (t < HD) part[2 + t] = A;
+    if (t == 0) {
+      part[0] = M;
+      part[1] = L;
+    }
+    __threadfence();
+    __syncthreads();
+    if (t == 0) last = atomicAdd(p.tickets + bh, 1u) == (unsigned)p.splits - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // The last CTA of this (stream, head) merges the chunks: scale factors in shared memory
+    // first, then every output dim sums its column with all loads in flight.
+    const float* parts = p.part + bh * p.splits * (HD + 2);
+    __shared__ float sc[kMaxSplits];
+    __shared__ float sl[kMaxSplits];
+    __shared__ float s_ll;
+    if (t < p.splits) {
+      sc[t] = __ldcg(parts + t * (HD + 2));
+      sl[t] = __ldcg(parts + t * (HD + 2) + 1);
+    }
+    __syncthreads();
+    if (t == 0) {
+      float MM = -INFINITY;
+      for (int s = 0; s < p.splits; s++) MM = fmaxf(MM, sc[s]);
+      float LL = 0.f;
+      for (int s = 0; s < p.splits; s++) {
+        const float c = sc[s] == -INFINITY ? 0.f : exp_ref(sc[s] - MM);
+        sc[s] = c;
+        LL = LL + sl[s] * c;
+      }
+      s_ll = LL;
+    }
+    __syncthreads();
+    if (t < HD) {
+      float AA = 0.f;
+#pragma unroll 4
+      for (int s = 0; s < p.splits; s++) AA = AA + __ldcg(parts + s * (HD + 2) + 2 + t) * sc[s];
+      so[t] = AA / s_ll;
+    }
+    if (t == 0) p.tickets[bh] = 0u;
   }
-  float* part = p.part + (bh * p.splits + split) * (HD + 2);
-  if (t < HD) part[2 + t] = A;
-  if (t == 0) {
-    part[0] = M;
-    part[1] = L;
-  }
-  __threadfence();
   __syncthreads();
-  if (t == 0) last = atomicAdd(p.tickets + bh, 1u) == (unsigned)p.splits - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  const float* parts = p.part + bh * p.splits * (HD + 2);
-  float MM = -INFINITY;
-  for (int s = 0; s < p.splits; s++) MM = fmaxf(MM, __ldcg(parts + s * (HD + 2)));
-  float LL = 0.f, AA = 0.f;
-  for (int s = 0; s < p.splits; s++) {
-    float ms = __ldcg(parts + s * (HD + 2));
-    if (ms == -INFINITY) continue;
-    float c = exp_ref(ms - MM);
-    LL = LL + __ldcg(parts + s * (HD + 2) + 1) * c;
-    if (t < HD) AA = AA + __ldcg(parts + s * (HD + 2) + 2 + t) * c;
-  }
-  if (t < HD) p.out[bh * HD + t] = AA / LL;
-  if (t == 0) p.tickets[bh] = 0u;
+  if (t < HD) p.out[bh * HD + t] = so[t];
 }
 
 template <int HD>
 void launch_hd(const AttnParams& p, cudaStream_t s) {
-  dim3 grid(p.splits, p.heads, p.nb);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits, p.heads, p.nb);
+  cfg.blockDim = dim3(kAttnWarps * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (p.kv_bf16)
-    attn_decode_kernel<HD, true><<<grid, kAttnWarps * 32, 0, s>>>(p);
+    cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, true>, p);
   else
-    attn_decode_kernel<HD, false><<<grid, kAttnWarps * 32, 0, s>>>(p);
+    cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, false>, p);
 }
 
 }  // namespace
+
+int attention_max_splits() { return kMaxSplits; }
 
 void launch_attention_decode(const AttnParams& p, cudaStream_t s) {
   switch (p.head_dim) {

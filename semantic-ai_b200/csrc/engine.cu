@@ -297,7 +297,7 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     // Split the keys of a (stream, head) so that batch 1 still covers the SMs.
     const int units = max_batch * c.num_heads;
     int splits = (2 * 148 + units - 1) / units;
-    splits = std::max(1, std::min(splits, (s->cap + 31) / 32));
+    splits = std::max(1, std::min({splits, (s->cap + 31) / 32, attention_max_splits()}));
     s->splits = splits;
     s->part.alloc((int64_t)max_batch * c.num_heads * splits * (c.head_dim + 2) * 4);
     s->tickets.alloc((int64_t)max_batch * c.num_heads * 4);
@@ -308,6 +308,7 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     check_cuda(cudaMemsetAsync(s->am_ticket.p, 0, 4, m->stream), "memset");
     s->err.alloc(4);
     check_cuda(cudaMemsetAsync(s->err.p, 0, 4, m->stream), "memset");
+
     if (m->kind == 0) {
       const auto& st = m->stt;
       s->logits.alloc((int64_t)max_batch * st.text_card * 4);
@@ -356,6 +357,19 @@ void set_norm(GemvParams& p, const Norm& N) {
   p.eps = N.eps;
 }
 
+// L2 prefetch of the next layer's copy of a matrix while this layer runs, when a whole
+// layer fits in a half of L2 beside the one being consumed.
+void set_prefetch(GemvParams& g, const Model& m, int l, const Linear& (*pick)(const Layer&)) {
+  const int L = (int)m.layers.size();
+  if (l + 1 >= L) return;
+  const Layer& cur = m.layers[l];
+  const int64_t layer_bytes = cur.in_proj.bytes() + cur.out_proj.bytes() + cur.ff1.bytes() + cur.ff2.bytes();
+  if (layer_bytes > 64ll * 1024 * 1024) return;
+  const Linear& nx = pick(m.layers[l + 1]);
+  g.pf = nx.w.as<uint8_t>();
+  g.pf_bytes = nx.row_stride * nx.n;
+}
+
 }  // namespace
 
 void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bool do_lin,
@@ -395,6 +409,7 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g.v_ring = vr;
     g.ring_stream_stride = s.ring_stream_stride;
     g.kv_bf16 = s.kv_elt == 2;
+    set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.in_proj; });
     if (do_lin) launch_gemv(g, st);
     // Sliding-window attention (nn/kernels/attention.rs:81-169).
     AttnParams a{};
@@ -423,6 +438,7 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g.out = x;
     g.out_stride = d;
     g.ls = L.ls1.as<float>();
+    set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.out_proj; });
     launch_gemv(g, st);
     // norm2 + feed-forward (nn/transformer.rs:438-464).
     g = gemv_base(L.ff1, x, d, nb);
@@ -431,18 +447,37 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g.out_stride = c.ffn_hidden;
     g.epi = c.ffn_kind == SVL_FFN_GATED_SILU ? EPI_SWIGLU
             : c.ffn_kind == SVL_FFN_PLAIN_GELU_ERF ? EPI_GELU_ERF : EPI_GELU_TANH;
+    set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.ff1; });
     launch_gemv(g, st);
     g = gemv_base(L.ff2, act, c.ffn_hidden, nb);
     g.epi = EPI_RESIDUAL;
     g.out = x;
     g.out_stride = d;
     g.ls = L.ls2.as<float>();
+    set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.ff2; });
     launch_gemv(g, st);
   }
 }
 
 void launch_extra_heads(const float* logits, int nb, int heads, int dim, float* out,
                         cudaStream_t st);
+
+namespace {
+
+GemvParams head_params(Model& m, State& s, int nb) {
+  GemvParams g = gemv_base(m.text_linear, s.x.as<float>(), m.cfg.d_model, nb);
+  set_norm(g, m.out_norm);
+  g.epi = EPI_LOGITS;
+  g.out = s.logits.as<float>();
+  g.out_stride = m.stt.text_card;
+  g.am_val = s.am_val.as<float>();
+  g.am_idx = s.am_idx.as<int>();
+  g.am_ticket = s.am_ticket.as<unsigned>();
+  g.tokens = s.tok_out.as<uint32_t>();
+  return g;
+}
+
+}  // namespace
 
 void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
   const auto& c = m.cfg;
@@ -462,18 +497,12 @@ void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
   e.error_flag = s.err.as<int>();
   launch_embed(e, st);
   enqueue_layers(m, s, 0, nb, st);
-  // out_norm + text_linear + argmax (stt/model.rs:252-258).
-  GemvParams g = gemv_base(m.text_linear, s.x.as<float>(), d, nb);
-  set_norm(g, m.out_norm);
-  g.epi = EPI_LOGITS;
-  g.out = s.logits.as<float>();
-  g.out_stride = m.stt.text_card;
-  g.am_val = s.am_val.as<float>();
-  g.am_idx = s.am_idx.as<int>();
-  g.am_ticket = s.am_ticket.as<unsigned>();
-  g.tokens = s.tok_out.as<uint32_t>();
+  // out_norm + text_linear + argmax (stt/model.rs:252-258). The step's last reader of the
+  // positions is done once the argmax is final: the argmax's last CTA advances them.
+  GemvParams g = head_params(m, s, nb);
+  g.pos_advance = s.pos.as<int>();
   launch_gemv(g, st);
-  // Extra (VAD) heads: softmax p[0] of each (stt/model.rs:259-271).
+  // Extra (VAD) heads: softmax p[0] of each (stt/model.rs:259-271); never quantised.
   const int eh = m.stt.extra_heads_num, edim = m.stt.extra_heads_dim;
   for (int i = 0; i < eh; i++) {
     GemvParams h = gemv_base(m.extra[i], s.x.as<float>(), d, nb);
@@ -484,7 +513,6 @@ void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
     launch_gemv(h, st);
   }
   if (eh > 0) launch_extra_heads(s.extra_logits.as<float>(), nb, eh, edim, s.extra_p.as<float>(), st);
-  launch_advance_positions(s.pos.as<int>(), nb, st);
 }
 
 void launch_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
@@ -513,16 +541,7 @@ int64_t enqueue_profile(Model& m, State& s, int nb, int which, cudaStream_t st) 
   const auto& c = m.cfg;
   if (which == 0) {
     enqueue_layers_mask(m, s, 0, nb, st, true, false);
-    GemvParams g = gemv_base(m.text_linear, s.x.as<float>(), c.d_model, nb);
-    set_norm(g, m.out_norm);
-    g.epi = EPI_LOGITS;
-    g.out = s.logits.as<float>();
-    g.out_stride = m.text_linear.n;
-    g.am_val = s.am_val.as<float>();
-    g.am_idx = s.am_idx.as<int>();
-    g.am_ticket = s.am_ticket.as<unsigned>();
-    g.tokens = s.tok_out.as<uint32_t>();
-    launch_gemv(g, st);
+    launch_gemv(head_params(m, s, nb), st);
     int64_t bytes = m.text_linear.bytes();
     for (const Layer& L : m.layers)
       bytes += L.in_proj.bytes() + L.out_proj.bytes() + L.ff1.bytes() + L.ff2.bytes();

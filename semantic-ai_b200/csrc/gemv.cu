@@ -1,12 +1,18 @@
 // gemv.cu — weight-streaming matrix-vector products for small stream counts.
 //
-// At batch 1 the step is bound by reading every weight once (nn/mod.rs:91-99 runs the
-// same product on the CPU through kernels::matvec, nn/kernels/matvec.rs:29-58). Each CTA
-// first applies the layer's norm to the input row(s) and converts them for the weight
-// format (bf16 rounding, or Q8_0 / Q8_1 blocks as candle's QMatMul quantises the
-// activation), then its warps stream groups of R rows with 16-byte loads, U loads per row
-// in flight, and finish each group with a fused epilogue (RoPE + KV-ring write, SwiGLU,
-// GELU, residual add, logits + argmax).
+// At small batch the step is bound by reading every weight once (the reference runs the
+// same products on the CPU through kernels::matvec, nn/kernels/matvec.rs:29-58, and
+// candle's QMatMul, nn/mod.rs:97). Each warp owns a contiguous range of row groups (R rows)
+// and streams them straight from global memory into registers, 16 bytes per lane and U
+// loads per row in flight, with 2 CTAs of 8 warps per SM, so about 64 KB per SM is in
+// flight. With programmatic dependent launch, each warp issues its first group's loads
+// before griddepcontrol.wait (weights do not depend on the previous kernel), and one thread
+// per CTA pulls its share of a later kernel's weights into L2 (cp.async.bulk.prefetch.L2).
+// After the wait, every CTA turns the input row(s) into records in shared memory -- the
+// layer's norm (candle rms_norm / layer_norm) and the conversion for the weight format
+// (bf16 rounding, or the Q8_0 / Q8_1 activation blocks candle's QMatMul builds) -- while
+// those first weight loads are still in flight. Each row group ends with the fused epilogue
+// (RoPE + KV-ring write, SwiGLU, GELU, SiLU, residual add, logits + argmax).
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -18,14 +24,28 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr int kCtasPerSm = 2;
+constexpr int kGrid = 148 * kCtasPerSm;
 
-template <int WT> struct Tile;
-template <> struct Tile<W_F32> { static constexpr int R = 2, U = 8; };
-template <> struct Tile<W_BF16> { static constexpr int R = 4, U = 4; };
-template <> struct Tile<W_Q8> { static constexpr int R = 4, U = 4; };
-template <> struct Tile<W_Q4> { static constexpr int R = 4, U = 4; };
+__device__ __forceinline__ uint4 ldg_weights(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// 16-byte chunks per row for each format.
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  if (v != v) return false;
+  if (bi == INT_MAX) return true;
+  return v > bv || (v == bv && i < bi);
+}
+
 __host__ __device__ inline int chunks_per_row(int wt, int k) {
   switch (wt) {
     case W_F32: return k / 4;
@@ -35,325 +55,401 @@ __host__ __device__ inline int chunks_per_row(int wt, int k) {
   }
 }
 
-__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
-  if (v != v) return false;
-  if (bi == INT_MAX) return true;
-  return v > bv || (v == bv && i < bi);
+// The fused epilogue for row `row` of stream b (value v; v_pair is the other row of the
+// aligned pair, for RoPE and SwiGLU).
+__device__ __forceinline__ void epilogue(const GemvParams& p, int b, int row, float v, float v_lo,
+                                         float v_hi) {
+  switch (p.epi) {
+    case EPI_STORE:
+    case EPI_LOGITS:
+      if (p.out) p.out[b * p.out_stride + row] = v + (p.bias ? p.bias[row] : 0.f);
+      break;
+    case EPI_RESIDUAL: {
+      float u = p.bias ? v + p.bias[row] : v;
+      if (p.ls) u = u * p.ls[row];
+      float* o = p.out + b * p.out_stride + row;
+      *o = *o + u;
+      break;
+    }
+    case EPI_GELU_TANH:
+      p.out[b * p.out_stride + row] = gelu_tanh_ref(p.bias ? v + p.bias[row] : v);
+      break;
+    case EPI_GELU_ERF:
+      p.out[b * p.out_stride + row] = gelu_erf_ref(p.bias ? v + p.bias[row] : v);
+      break;
+    case EPI_SILU:
+      p.out[b * p.out_stride + row] = silu_ref(p.bias ? v + p.bias[row] : v);
+      break;
+    case EPI_SWIGLU:
+      // Packed row 2i is gate row i, 2i+1 value row i (FeedForwardLayer::Gated,
+      // nn/transformer.rs:457-461).
+      if (!(row & 1)) p.out[b * p.out_stride + row / 2] = silu_ref(v_lo) * v_hi;
+      break;
+    case EPI_QKV_ROPE: {
+      const int hd = p.head_dim;
+      const int pos = p.pos[b];
+      const int slot = p.windowed ? pos % p.ring_cap : pos;
+      if (row < p.q_dim + p.kv_dim) {
+        // rope_i (candle; nn/transformer.rs:339-340): pairs (2i, 2i+1) rotate by pos * f_i.
+        const int dim = row % hd, i = dim >> 1;
+        float sn, cs;
+        sincosf((float)pos * p.inv_freq[i], &sn, &cs);
+        const float val = (dim & 1) ? v_lo * sn + v_hi * cs : v_lo * cs - v_hi * sn;
+        if (row < p.q_dim) {
+          p.out[b * p.out_stride + row] = val;
+        } else {
+          const int kh = (row - p.q_dim) / hd;
+          const int64_t off = b * p.ring_stream_stride + ((int64_t)kh * p.ring_cap + slot) * hd + dim;
+          if (p.kv_bf16)
+            reinterpret_cast<__nv_bfloat16*>(p.k_ring)[off] = __float2bfloat16_rn(val);
+          else
+            reinterpret_cast<float*>(p.k_ring)[off] = val;
+        }
+      } else {
+        const int vr = row - p.q_dim - p.kv_dim;
+        const int kh = vr / hd, dim = vr % hd;
+        const int64_t off = b * p.ring_stream_stride + ((int64_t)kh * p.ring_cap + slot) * hd + dim;
+        if (p.kv_bf16)
+          reinterpret_cast<__nv_bfloat16*>(p.v_ring)[off] = __float2bfloat16_rn(v);
+        else
+          reinterpret_cast<float*>(p.v_ring)[off] = v;
+      }
+      break;
+    }
+  }
 }
 
-__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+// Input record of one stream in shared memory. F32 / BF16: k f32 (bf16-rounded for BF16).
+// Q8 / Q4: k int8 (Q8_0 / Q8_1 activation blocks), then k/32 f32 scales d, then (Q4) k/32
+// f32 block sums s = d * sum(q). Padded to 16 bytes.
+__host__ __device__ inline int rec_bytes_of(int wtype, int k) {
+  const int b = (wtype == W_F32 || wtype == W_BF16) ? k * 4 : k + (k / QBLK) * 4 * (wtype == W_Q4 ? 2 : 1);
+  return (b + 15) / 16 * 16;
+}
 
+constexpr int kMaxGroupsPerThread = 5;  // 8-element groups per thread: k <= 256 * 8 * 5
+
+// Builds the NB input records from the raw rows p.x: thread t owns the 8-element groups
+// t, t + 256, ... (so the four groups of a 32-element block sit on four adjacent lanes).
 template <int WT, int NB>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
-  constexpr int R = Tile<WT>::R;
-  constexpr int U = Tile<WT>::U;
-  extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ float red_a[kWarps][NB], red_b[kWarps][NB];
-  __shared__ float stat_a[NB], stat_b[NB];
-  __shared__ float am_v[kWarps][NB];
-  __shared__ int am_i[kWarps][NB];
-  __shared__ bool am_last;
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int k = p.k;
-  const int nb = p.nb;
-
-  // ---- prologue 1: norm statistics of each input row.
-  if (p.norm != NORM_NONE) {
-    float s[NB], s2[NB];
+__device__ __forceinline__ void build_records(const GemvParams& p, uint8_t* xsm, int rec,
+                                              float (*red)[kWarps], float* stat) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, k = p.k, ngr = k / 8, nblk = k / QBLK;
+  for (int b = 0; b < NB; b++) {
+    if (b >= p.nb) break;
+    float v[kMaxGroupsPerThread][8];
+    const float* x = p.x + b * p.x_stride;
 #pragma unroll
-    for (int b = 0; b < NB; b++) {
-      s[b] = 0.f;
-      s2[b] = 0.f;
-      if (b < nb) {
-        const float* x = p.x + b * p.x_stride;
-        for (int i = tid; i < k; i += kThreads) {
-          float v = x[i];
-          s[b] += v;
-          s2[b] += v * v;
-        }
+    for (int j = 0; j < kMaxGroupsPerThread; j++) {
+      const int g = t + j * kThreads;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
+      if (g < ngr) {
+        a = __ldcg(reinterpret_cast<const float4*>(x + g * 8));
+        c = __ldcg(reinterpret_cast<const float4*>(x + g * 8) + 1);
       }
-      s[b] = warp_sum(s[b]);
-      s2[b] = warp_sum(s2[b]);
+      v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
+      v[j][4] = c.x; v[j][5] = c.y; v[j][6] = c.z; v[j][7] = c.w;
+    }
+    if (p.norm != NORM_NONE) {
+      float s = 0.f, s2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < kMaxGroupsPerThread; j++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          s += v[j][e];
+          s2 += v[j][e] * v[j][e];
+        }
+      s = warp_sum(s);
+      s2 = warp_sum(s2);
       if (lane == 0) {
-        red_a[warp][b] = s[b];
-        red_b[warp][b] = s2[b];
+        red[0][warp] = s;
+        red[1][warp] = s2;
       }
-    }
-    __syncthreads();
-    if (tid < NB) {
-      float a = 0.f, c = 0.f;
-      for (int w = 0; w < kWarps; w++) {
-        a += red_a[w][tid];
-        c += red_b[w][tid];
-      }
-      if (p.norm == NORM_RMS) {
-        // candle rms_norm: m = sqrt(sum(x^2) / d + eps)
-        stat_a[tid] = sqrtf(c / (float)k + p.eps);
-      } else {
-        // candle layer_norm: var = E[x^2] - mean^2, inv_std = 1 / sqrt(var + eps)
-        float mean = a / (float)k;
-        float var = c / (float)k - mean * mean;
-        stat_a[tid] = mean;
-        stat_b[tid] = 1.0f / sqrtf(var + p.eps);
-      }
-    }
-    __syncthreads();
-  }
-
-  auto normed = [&](int b, int i) -> float {
-    float v = p.x[b * p.x_stride + i];
-    if (p.norm == NORM_RMS) {
-      v = v / stat_a[b] * p.norm_w[i];
-    } else if (p.norm == NORM_LAYER) {
-      v = (v - stat_a[b]) * stat_b[b] * p.norm_w[i] + p.norm_b[i];
-    }
-    return v;
-  };
-
-  // ---- prologue 2: the converted input rows in shared memory.
-  float* xs = reinterpret_cast<float*>(smem);                     // F32 / BF16: [NB][k]
-  int8_t* xq = reinterpret_cast<int8_t*>(smem);                   // Q8 / Q4: [NB][k]
-  float* xd = reinterpret_cast<float*>(smem + (size_t)NB * k);    // [NB][k/32]
-  float* xsum = xd + (size_t)NB * (k / QBLK);                     // [NB][k/32] (Q4 only)
-  if (WT == W_F32 || WT == W_BF16) {
-    for (int b = 0; b < NB; b++)
-      for (int i = tid; i < k; i += kThreads) {
-        float v = b < nb ? normed(b, i) : 0.f;
-        xs[b * k + i] = WT == W_BF16 ? round_bf16(v) : v;
-      }
-  } else {
-    const int nblk = k / QBLK;
-    for (int b = 0; b < NB; b++)
-      for (int blk = warp; blk < nblk; blk += kWarps) {
-        float v = b < nb ? normed(b, blk * QBLK + lane) : 0.f;
-        // ggml/candle Q8_0 (and Q8_1) block: d = amax / 127, q = round(x * (1 / d)).
-        float amax = warp_max(fabsf(v));
-        float d = amax / 127.0f;
-        float id = d != 0.0f ? 1.0f / d : 0.0f;
-        int q = (int)roundf(v * id);
-        xq[b * k + blk * QBLK + lane] = (int8_t)q;
-        if (WT == W_Q4) {
-          int sum = warp_sum_int(q);
-          if (lane == 0) xsum[b * nblk + blk] = f16_round((float)sum * d);
+      __syncthreads();
+      if (t == 0) {
+        float a = 0.f, c = 0.f;
+        for (int w = 0; w < kWarps; w++) {
+          a += red[0][w];
+          c += red[1][w];
         }
-        if (lane == 0) xd[b * nblk + blk] = f16_round(d);
+        if (p.norm == NORM_RMS) {
+          stat[0] = sqrtf(c / (float)k + p.eps);  // candle rms_norm: sqrt(mean(x^2) + eps)
+        } else {
+          const float mean = a / (float)k;        // candle layer_norm: E[x^2] - mean^2
+          const float var = c / (float)k - mean * mean;
+          stat[0] = mean;
+          stat[1] = 1.0f / sqrtf(var + p.eps);
+        }
       }
+      __syncthreads();
+    }
+    uint8_t* r = xsm + (size_t)b * rec;
+#pragma unroll
+    for (int j = 0; j < kMaxGroupsPerThread; j++) {
+      if (j * kThreads >= ngr) break;
+      const int g = t + j * kThreads;
+      const bool on = g < ngr;
+      const int i0 = (on ? g : 0) * 8;
+      float* vv = v[j];
+      if (p.norm != NORM_NONE) {
+        const float4 wa = reinterpret_cast<const float4*>(p.norm_w + i0)[0];
+        const float4 wc = reinterpret_cast<const float4*>(p.norm_w + i0)[1];
+        const float w8[8] = {wa.x, wa.y, wa.z, wa.w, wc.x, wc.y, wc.z, wc.w};
+        if (p.norm == NORM_RMS) {
+#pragma unroll
+          for (int e = 0; e < 8; e++) vv[e] = vv[e] / stat[0] * w8[e];
+        } else {
+          const float4 ba = reinterpret_cast<const float4*>(p.norm_b + i0)[0];
+          const float4 bc = reinterpret_cast<const float4*>(p.norm_b + i0)[1];
+          const float b8[8] = {ba.x, ba.y, ba.z, ba.w, bc.x, bc.y, bc.z, bc.w};
+#pragma unroll
+          for (int e = 0; e < 8; e++) vv[e] = (vv[e] - stat[0]) * stat[1] * w8[e] + b8[e];
+        }
+      }
+      if (WT == W_F32 || WT == W_BF16) {
+        if (on) {
+          if (WT == W_BF16)
+#pragma unroll
+            for (int e = 0; e < 8; e++) vv[e] = round_bf16(vv[e]);
+          float4* dst = reinterpret_cast<float4*>(r + (size_t)i0 * 4);
+          dst[0] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+          dst[1] = make_float4(vv[4], vv[5], vv[6], vv[7]);
+        }
+      } else {
+        // ggml/candle activation block: d = amax / 127, q = round(x * (1 / d)).
+        float amax = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(vv[e]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        int sum = 0;
+        uint32_t w2[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const int q = (int)roundf(vv[4 * h + e] * id);
+            sum += q;
+            word |= ((uint32_t)q & 0xffu) << (8 * e);
+          }
+          w2[h] = word;
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (on) {
+          *reinterpret_cast<uint2*>(r + i0) = make_uint2(w2[0], w2[1]);
+          if ((g & 3) == 0) {
+            float* dd = reinterpret_cast<float*>(r + k);
+            dd[g >> 2] = f16_round(d);
+            if (WT == W_Q4) dd[nblk + (g >> 2)] = f16_round((float)sum * d);
+          }
+        }
+      }
+    }
   }
   __syncthreads();
+}
 
-  // ---- main loop: groups of R rows per warp.
-  const int nch = chunks_per_row(WT, k);
+// Accumulates chunks [c0, c0 + 32 U) of R rows (weights already in wv) against the NB input
+// records in shared memory (record b at xsm + b * rec: see input_rec_bytes).
+template <int WT, int NB, int R, int U>
+__device__ __forceinline__ void dot_chunks(const uint4 (&wv)[R][U], const GemvParams& p, int g, int c0,
+                                           const uint8_t* xsm, int rec, int lane, float (&acc)[R][NB]) {
+  const int k = p.k, nch = chunks_per_row(WT, k), nblk = k / QBLK;
+#pragma unroll
+  for (int u = 0; u < U; u++) {
+    const int c = c0 + lane + 32 * u;
+    const bool valid = c < nch;
+    if (WT == W_F32) {
+      if (valid) {
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+          const float4 x = reinterpret_cast<const float4*>(xsm + (size_t)b * rec)[c];
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+            const float4 w = *reinterpret_cast<const float4*>(&wv[r][u]);
+            float a = acc[r][b];
+            a = fmaf(w.x, x.x, a);
+            a = fmaf(w.y, x.y, a);
+            a = fmaf(w.z, x.z, a);
+            a = fmaf(w.w, x.w, a);
+            acc[r][b] = a;
+          }
+        }
+      }
+    } else if (WT == W_BF16) {
+      if (valid) {
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+          const float4 x0 = reinterpret_cast<const float4*>(xsm + (size_t)b * rec)[2 * c];
+          const float4 x1 = reinterpret_cast<const float4*>(xsm + (size_t)b * rec)[2 * c + 1];
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+            const uint4 w = wv[r][u];
+            float a = acc[r][b];
+            a = fmaf(bf16_lo(w.x), x0.x, a);
+            a = fmaf(bf16_hi(w.x), x0.y, a);
+            a = fmaf(bf16_lo(w.y), x0.z, a);
+            a = fmaf(bf16_hi(w.y), x0.w, a);
+            a = fmaf(bf16_lo(w.z), x1.x, a);
+            a = fmaf(bf16_hi(w.z), x1.y, a);
+            a = fmaf(bf16_lo(w.w), x1.z, a);
+            a = fmaf(bf16_hi(w.w), x1.w, a);
+            acc[r][b] = a;
+          }
+        }
+      }
+    } else if (WT == W_Q8) {
+      // Chunk c is half of block c/2: lanes 2j and 2j+1 share a block and its scales.
+      const int blk = c >> 1;
+      float dw[R];
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const int row = g * R + r;
+        dw[r] = (valid && row < p.n) ? __half2float(reinterpret_cast<const __half*>(p.w + (int64_t)row * p.row_stride + k)[blk]) : 0.f;
+      }
+#pragma unroll
+      for (int b = 0; b < NB; b++) {
+        const uint8_t* xr = xsm + (size_t)b * rec;
+        const int4 x = valid ? reinterpret_cast<const int4*>(xr)[c] : make_int4(0, 0, 0, 0);
+        const float dx = valid ? reinterpret_cast<const float*>(xr + k)[blk] : 0.f;
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          const uint4 w = wv[r][u];
+          int s = __dp4a((int)w.x, x.x, 0);
+          s = __dp4a((int)w.y, x.y, s);
+          s = __dp4a((int)w.z, x.z, s);
+          s = __dp4a((int)w.w, x.w, s);
+          s += __shfl_xor_sync(0xffffffffu, s, 1);
+          if (valid && !(lane & 1)) acc[r][b] = fmaf(dw[r] * dx, (float)s, acc[r][b]);
+        }
+      }
+    } else {  // W_Q4: chunk c is block c, 16 bytes of nibbles (ggml Q4_1 order).
+      if (valid) {
+        float2 dm[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          const int row = g * R + r;
+          dm[r] = row < p.n ? __half22float2(reinterpret_cast<const __half2*>(p.w + (int64_t)row * p.row_stride + k / 2)[c])
+                            : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+          const uint8_t* xr = xsm + (size_t)b * rec;
+          const int4* xb = reinterpret_cast<const int4*>(xr + (size_t)c * QBLK);
+          const int4 lo = xb[0], hi = xb[1];
+          const float dx = reinterpret_cast<const float*>(xr + k)[c];
+          const float sx = reinterpret_cast<const float*>(xr + k)[nblk + c];
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+            const uint4 w = wv[r][u];
+            int s = __dp4a((int)(w.x & 0x0f0f0f0fu), lo.x, 0);
+            s = __dp4a((int)(w.y & 0x0f0f0f0fu), lo.y, s);
+            s = __dp4a((int)(w.z & 0x0f0f0f0fu), lo.z, s);
+            s = __dp4a((int)(w.w & 0x0f0f0f0fu), lo.w, s);
+            s = __dp4a((int)((w.x >> 4) & 0x0f0f0f0fu), hi.x, s);
+            s = __dp4a((int)((w.y >> 4) & 0x0f0f0f0fu), hi.y, s);
+            s = __dp4a((int)((w.z >> 4) & 0x0f0f0f0fu), hi.z, s);
+            s = __dp4a((int)((w.w >> 4) & 0x0f0f0f0fu), hi.w, s);
+            acc[r][b] += (dm[r].x * dx) * (float)s + dm[r].y * sx;
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int WT, int NB, int R, int U>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(16) uint8_t xsm[];
+  __shared__ float am_v[kWarps][NB];
+  __shared__ int am_i[kWarps][NB];
+  __shared__ float red[2][kWarps];
+  __shared__ float stat[2];
+  __shared__ bool last_cta;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nb = p.nb, nch = chunks_per_row(WT, p.k), rec = rec_bytes_of(WT, p.k);
+  // Row groups of R rows (R even keeps the RoPE / SwiGLU pairs in one group), split into
+  // contiguous ranges per warp.
   const int groups = (p.n + R - 1) / R;
+  const int total_w = gridDim.x * kWarps;
+  const int gw = blockIdx.x * kWarps + warp;
+  const int g0 = (int)((int64_t)gw * groups / total_w), g1 = (int)((int64_t)(gw + 1) * groups / total_w);
+
+  uint4 wv[R][U];
+  auto issue = [&](int g, int c0) {
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int c = c0 + lane + 32 * u;
+        const int row = g * R + r;
+        wv[r][u] = (g < g1 && c < nch && row < p.n)
+                       ? ldg_weights(p.w + (int64_t)row * p.row_stride + (int64_t)c * 16)
+                       : make_uint4(0, 0, 0, 0);
+      }
+  };
+  // Weights do not depend on the previous kernel: first group's loads and the L2 prefetch
+  // of a later kernel's weights go out before the dependency wait.
+  issue(g0, 0);
+  if (tid == 0 && p.pf && p.pf_bytes > 0) {
+    const int64_t share = (p.pf_bytes / gridDim.x + 15) / 16 * 16;
+    const int64_t a = (int64_t)blockIdx.x * share;
+    const int64_t e = min(a + share, p.pf_bytes / 16 * 16);
+    for (int64_t o = a; o < e; o += 65536) prefetch_l2(p.pf + o, (uint32_t)(e - o < 65536 ? e - o : 65536));
+  }
+  pdl_launch();
+  pdl_wait();
+  build_records<WT, NB>(p, xsm, rec, red, stat);
+
   float best_v = 0.f;
   int best_i = INT_MAX;
-
-  for (int g = blockIdx.x * kWarps + warp; g < groups; g += gridDim.x * kWarps) {
-    const int r0 = g * R;
+  for (int g = g0; g < g1; g++) {
     float acc[R][NB];
 #pragma unroll
     for (int r = 0; r < R; r++)
 #pragma unroll
       for (int b = 0; b < NB; b++) acc[r][b] = 0.f;
-
     for (int c0 = 0; c0 < nch; c0 += 32 * U) {
-      uint4 wv[R][U];
-#pragma unroll
-      for (int r = 0; r < R; r++)
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-          int c = c0 + lane + 32 * u;
-          if (c < nch && r0 + r < p.n)
-            wv[r][u] = ldg_stream(p.w + (int64_t)(r0 + r) * p.row_stride + (int64_t)c * 16);
-          else
-            wv[r][u] = make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        const int c = c0 + lane + 32 * u;
-        const bool valid = c < nch;
-        if (WT == W_F32) {
-          if (valid) {
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-              float4 xv = reinterpret_cast<const float4*>(xs + b * k)[c];
-#pragma unroll
-              for (int r = 0; r < R; r++) {
-                float4 w = *reinterpret_cast<float4*>(&wv[r][u]);
-                acc[r][b] = fmaf(w.x, xv.x, acc[r][b]);
-                acc[r][b] = fmaf(w.y, xv.y, acc[r][b]);
-                acc[r][b] = fmaf(w.z, xv.z, acc[r][b]);
-                acc[r][b] = fmaf(w.w, xv.w, acc[r][b]);
-              }
-            }
-          }
-        } else if (WT == W_BF16) {
-          if (valid) {
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-              float4 x0 = reinterpret_cast<const float4*>(xs + b * k)[2 * c];
-              float4 x1 = reinterpret_cast<const float4*>(xs + b * k)[2 * c + 1];
-#pragma unroll
-              for (int r = 0; r < R; r++) {
-                uint4 w = wv[r][u];
-                float a = acc[r][b];
-                a = fmaf(bf16_lo(w.x), x0.x, a);
-                a = fmaf(bf16_hi(w.x), x0.y, a);
-                a = fmaf(bf16_lo(w.y), x0.z, a);
-                a = fmaf(bf16_hi(w.y), x0.w, a);
-                a = fmaf(bf16_lo(w.z), x1.x, a);
-                a = fmaf(bf16_hi(w.z), x1.y, a);
-                a = fmaf(bf16_lo(w.w), x1.z, a);
-                a = fmaf(bf16_hi(w.w), x1.w, a);
-                acc[r][b] = a;
-              }
-            }
-          }
-        } else if (WT == W_Q8) {
-          // Chunk c holds half of block c/2; lanes 2j and 2j+1 share a block.
-          const int blk = c >> 1;
-          const int nblk = k / QBLK;
-#pragma unroll
-          for (int b = 0; b < NB; b++) {
-            int4 xv = valid ? reinterpret_cast<const int4*>(xq + b * k)[c] : make_int4(0, 0, 0, 0);
-            float dx = valid ? xd[b * nblk + blk] : 0.f;
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-              uint4 w = wv[r][u];
-              int s = dp4a((int)w.x, xv.x, 0);
-              s = dp4a((int)w.y, xv.y, s);
-              s = dp4a((int)w.z, xv.z, s);
-              s = dp4a((int)w.w, xv.w, s);
-              s += __shfl_xor_sync(0xffffffffu, s, 1);
-              if (valid && !(lane & 1) && r0 + r < p.n) {
-                const __half* scales = reinterpret_cast<const __half*>(
-                    p.w + (int64_t)(r0 + r) * p.row_stride + k);
-                float dd = __half2float(scales[blk]) * dx;
-                acc[r][b] = fmaf(dd, (float)s, acc[r][b]);
-              }
-            }
-          }
-        } else {  // W_Q4: chunk c is block c (16 bytes of nibbles, ggml Q4_1 order).
-          const int nblk = k / QBLK;
-          if (valid) {
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-              const int4* xb = reinterpret_cast<const int4*>(xq + b * k + c * QBLK);
-              int4 xlo = xb[0], xhi = xb[1];
-              float dx = xd[b * nblk + c], sx = xsum[b * nblk + c];
-#pragma unroll
-              for (int r = 0; r < R; r++) {
-                if (r0 + r >= p.n) continue;
-                uint4 w = wv[r][u];
-                int s = 0;
-                s = dp4a((int)(w.x & 0x0f0f0f0fu), xlo.x, s);
-                s = dp4a((int)(w.y & 0x0f0f0f0fu), xlo.y, s);
-                s = dp4a((int)(w.z & 0x0f0f0f0fu), xlo.z, s);
-                s = dp4a((int)(w.w & 0x0f0f0f0fu), xlo.w, s);
-                s = dp4a((int)((w.x >> 4) & 0x0f0f0f0fu), xhi.x, s);
-                s = dp4a((int)((w.y >> 4) & 0x0f0f0f0fu), xhi.y, s);
-                s = dp4a((int)((w.z >> 4) & 0x0f0f0f0fu), xhi.z, s);
-                s = dp4a((int)((w.w >> 4) & 0x0f0f0f0fu), xhi.w, s);
-                const __half2* dm = reinterpret_cast<const __half2*>(
-                    p.w + (int64_t)(r0 + r) * p.row_stride + k / 2);
-                float2 f = __half22float2(dm[c]);
-                acc[r][b] += (f.x * dx) * (float)s + f.y * sx;
-              }
-            }
-          }
-        }
-      }
+      if (c0 > 0) issue(g, c0);
+      dot_chunks<WT, NB, R, U>(wv, p, g, c0, xsm, rec, lane, acc);
     }
+    // The next group's first loads fly while this group reduces and runs its epilogue.
+    if (g + 1 < g1) issue(g + 1, 0);
 #pragma unroll
     for (int r = 0; r < R; r++)
 #pragma unroll
       for (int b = 0; b < NB; b++) acc[r][b] = warp_sum(acc[r][b]);
-
-    // ---- epilogue: lane j owns (row r0 + j / NB, stream j % NB).
+    const int row = g * R;
     if (p.epi == EPI_LOGITS && lane < NB && lane < nb) {
 #pragma unroll
       for (int r = 0; r < R; r++) {
-        int row = r0 + r;
-        if (row < p.n) {
-          float v = acc[r][lane] + (p.bias ? p.bias[row] : 0.f);
-          if (better(v, row, best_v, best_i)) {
+        float v = 0.f;
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+          if (b == lane) v = acc[r][b];
+        if (row + r < p.n) {
+          v = v + (p.bias ? p.bias[row + r] : 0.f);
+          if (better(v, row + r, best_v, best_i)) {
             best_v = v;
-            best_i = row;
+            best_i = row + r;
           }
         }
       }
     }
 #pragma unroll
-    for (int j = 0; j < R * NB; j++) {
-      if (lane != j) continue;
-      const int r = j / NB, b = j % NB, row = r0 + r;
-      if (b >= nb || row >= p.n) continue;
-      float v = acc[r][b];
-      switch (p.epi) {
-        case EPI_STORE:
-        case EPI_LOGITS:
-          if (p.out) p.out[b * p.out_stride + row] = v + (p.bias ? p.bias[row] : 0.f);
-          break;
-        case EPI_RESIDUAL: {
-          float u = p.bias ? v + p.bias[row] : v;
-          if (p.ls) u = u * p.ls[row];
-          float* o = p.out + b * p.out_stride + row;
-          *o = *o + u;
-          break;
-        }
-        case EPI_GELU_TANH:
-          p.out[b * p.out_stride + row] = gelu_tanh_ref(p.bias ? v + p.bias[row] : v);
-          break;
-        case EPI_GELU_ERF:
-          p.out[b * p.out_stride + row] = gelu_erf_ref(p.bias ? v + p.bias[row] : v);
-          break;
-        case EPI_SILU:
-          p.out[b * p.out_stride + row] = silu_ref(p.bias ? v + p.bias[row] : v);
-          break;
-        case EPI_SWIGLU:
-          if (!(r & 1)) {
-            float g = v, val = acc[r | 1][b];
-            p.out[b * p.out_stride + row / 2] = silu_ref(g) * val;
-          }
-          break;
-        case EPI_QKV_ROPE: {
-          const int hd = p.head_dim;
-          const int pos = p.pos[b];
-          if (row < p.q_dim + p.kv_dim) {
-            // rope_i (candle, used at nn/transformer.rs:339-340): pairs (2i, 2i+1).
-            const int dim = row % hd, i = dim >> 1;
-            const float a = acc[r & ~1][b], c2 = acc[r | 1][b];
-            float sn, cs;
-            sincosf((float)pos * p.inv_freq[i], &sn, &cs);
-            float val = (dim & 1) ? a * sn + c2 * cs : a * cs - c2 * sn;
-            if (row < p.q_dim) {
-              p.out[b * p.out_stride + row] = val;
-            } else {
-              const int kh = (row - p.q_dim) / hd;
-              const int slot = p.windowed ? pos % p.ring_cap : pos;
-              int64_t off = b * p.ring_stream_stride + ((int64_t)kh * p.ring_cap + slot) * hd + dim;
-              if (p.kv_bf16)
-                reinterpret_cast<__nv_bfloat16*>(p.k_ring)[off] = __float2bfloat16_rn(val);
-              else
-                reinterpret_cast<float*>(p.k_ring)[off] = val;
-            }
-          } else {
-            const int vr = row - p.q_dim - p.kv_dim;
-            const int kh = vr / hd, dim = vr % hd;
-            const int slot = p.windowed ? pos % p.ring_cap : pos;
-            int64_t off = b * p.ring_stream_stride + ((int64_t)kh * p.ring_cap + slot) * hd + dim;
-            if (p.kv_bf16)
-              reinterpret_cast<__nv_bfloat16*>(p.v_ring)[off] = __float2bfloat16_rn(v);
-            else
-              reinterpret_cast<float*>(p.v_ring)[off] = v;
-          }
-          break;
-        }
-      }
+    for (int jj = 0; jj < R * NB; jj++) {
+      const int r = jj / NB, b = jj % NB;
+      if (lane == jj && b < nb && row + r < p.n)
+        epilogue(p, b, row + r, acc[r][b], acc[r & ~1][b], acc[(r | 1) % R][b]);
     }
   }
 
-  // ---- argmax: CTA best, then the last CTA reduces the CTA bests.
+  // Argmax: CTA best per stream, then the last CTA reduces the CTA bests.
   if (p.epi == EPI_LOGITS) {
     if (lane < NB) {
       am_v[warp][lane] = best_v;
@@ -373,67 +469,109 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) am_last = atomicAdd(p.am_ticket, 1u) == gridDim.x - 1;
+    if (tid == 0) last_cta = atomicAdd(p.am_ticket, 1u) == gridDim.x - 1;
     __syncthreads();
-    if (am_last) {
+    if (last_cta) {
       __threadfence();
       if (tid < nb && tid < NB) {
         float bv = 0.f;
         int bi = INT_MAX;
         for (int g = 0; g < (int)gridDim.x; g++) {
-          float v = __ldcg(p.am_val + tid * gridDim.x + g);
-          int i = __ldcg(p.am_idx + tid * gridDim.x + g);
-          if (i != INT_MAX && better(v, i, bv, bi)) {
+          const float v = __ldcg(p.am_val + tid * gridDim.x + g);
+          const int ix = __ldcg(p.am_idx + tid * gridDim.x + g);
+          if (ix != INT_MAX && better(v, ix, bv, bi)) {
             bv = v;
-            bi = i;
+            bi = ix;
           }
         }
         p.tokens[tid] = bi == INT_MAX ? 0u : (uint32_t)bi;
+        if (p.pos_advance) p.pos_advance[tid] += 1;
       }
       if (tid == 0) *p.am_ticket = 0u;
     }
   }
+
 }
 
+constexpr size_t kMaxSmem = 96 * 1024;  // input records; 2 CTAs per SM
+
+// Rows per warp group: the fewest (of 1, 2, 4) whose groups fit in one wave of warps, so the
+// whole matrix is in flight at once; 2 at least when the epilogue pairs rows.
+int pick_r(const GemvParams& p) {
+  const int warps = kGrid * kWarps;
+  const bool pairs = p.epi == EPI_QKV_ROPE || p.epi == EPI_SWIGLU;
+  if (!pairs && p.n <= warps) return 1;
+  if (p.n <= 2 * warps) return 2;
+  return 4;
+}
+
+template <int WT, int NB, int R>
+void launch_r(const GemvParams& p, cudaStream_t s) {
+  constexpr int U = WT == W_F32 ? 8 : 4;
+  const int groups = (p.n + R - 1) / R;
+  int grid = (groups + kWarps - 1) / kWarps;
+  if (grid > kGrid) grid = kGrid;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = (size_t)NB * rec_bytes_of(WT, p.k);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, gemv_kernel<WT, NB, R, U>, p);
+}
+
+// Four-row groups only where their registers fit without spilling (one stream, 16-byte
+// formats with U = 4).
 template <int WT, int NB>
-size_t smem_bytes(int k) {
-  if (WT == W_F32 || WT == W_BF16) return (size_t)NB * k * 4;
-  return (size_t)NB * k + (size_t)NB * (k / QBLK) * 4 * (WT == W_Q4 ? 2 : 1);
-}
-
-constexpr size_t kMaxSmem = 200 * 1024;
+constexpr bool kAllowR4 = NB == 1 && WT != W_F32;
 
 template <int WT, int NB>
 void launch_t(const GemvParams& p, cudaStream_t s) {
-  constexpr int R = Tile<WT>::R;
-  size_t sm = smem_bytes<WT, NB>(p.k);
-  int groups = (p.n + R - 1) / R;
-  int grid = (groups + kWarps - 1) / kWarps;
-  int max_grid = p.epi == EPI_LOGITS ? kLogitsGrid : 2 * 148;
-  if (grid > max_grid) grid = max_grid;
-  gemv_kernel<WT, NB><<<grid, kThreads, sm, s>>>(p);
+  int r = pick_r(p);
+  if (!kAllowR4<WT, NB> && r == 4) r = 2;
+  if constexpr (kAllowR4<WT, NB>) {
+    if (r == 4) {
+      launch_r<WT, NB, 4>(p, s);
+      return;
+    }
+  }
+  if (r == 2)
+    launch_r<WT, NB, 2>(p, s);
+  else
+    launch_r<WT, NB, 1>(p, s);
+}
+
+template <int WT, int NB>
+void set_attrs_nb() {
+  constexpr int U = WT == W_F32 ? 8 : 4;
+  cudaFuncSetAttribute(gemv_kernel<WT, NB, 1, U>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  cudaFuncSetAttribute(gemv_kernel<WT, NB, 2, U>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  if constexpr (kAllowR4<WT, NB>)
+    cudaFuncSetAttribute(gemv_kernel<WT, NB, 4, U>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
 }
 
 template <int WT>
 void set_attrs() {
-  cudaFuncSetAttribute(gemv_kernel<WT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-  cudaFuncSetAttribute(gemv_kernel<WT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-  cudaFuncSetAttribute(gemv_kernel<WT, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-  cudaFuncSetAttribute(gemv_kernel<WT, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  set_attrs_nb<WT, 1>();
+  set_attrs_nb<WT, 2>();
+  set_attrs_nb<WT, 4>();
+  set_attrs_nb<WT, 8>();
 }
 
-// Streams per launch: the largest template width whose input rows fit in shared memory.
-template <int WT>
-int max_nb(int k) {
-  if (smem_bytes<WT, 8>(k) <= kMaxSmem) return 8;
-  if (smem_bytes<WT, 4>(k) <= kMaxSmem) return 4;
-  if (smem_bytes<WT, 2>(k) <= kMaxSmem) return 2;
+// Streams per launch: the widest template whose input records fit.
+int max_nb(const GemvParams& p) {
+  for (int nb : {8, 4, 2})
+    if ((size_t)nb * rec_bytes_of(p.wtype, p.k) <= kMaxSmem) return nb;
   return 1;
 }
 
 template <int WT>
 void launch_w(const GemvParams& p0, cudaStream_t s) {
-  const int cap = max_nb<WT>(p0.k);
+  const int cap = max_nb(p0);
   for (int b0 = 0; b0 < p0.nb; b0 += cap) {
     GemvParams p = p0;
     p.nb = p0.nb - b0 < cap ? p0.nb - b0 : cap;
@@ -441,11 +579,13 @@ void launch_w(const GemvParams& p0, cudaStream_t s) {
     if (p0.out) p.out = p0.out + b0 * p0.out_stride;
     if (p0.pos) p.pos = p0.pos + b0;
     if (p0.tokens) p.tokens = p0.tokens + b0;
+    if (p0.pos_advance) p.pos_advance = p0.pos_advance + b0;
     if (p0.k_ring) {
-      size_t el = p0.kv_bf16 ? 2 : 4;
+      const size_t el = p0.kv_bf16 ? 2 : 4;
       p.k_ring = static_cast<uint8_t*>(p0.k_ring) + b0 * p0.ring_stream_stride * el;
       p.v_ring = static_cast<uint8_t*>(p0.v_ring) + b0 * p0.ring_stream_stride * el;
     }
+    if (b0 > 0) p.pf = nullptr;
     switch (p.nb) {
       case 1: launch_t<WT, 1>(p, s); break;
       case 2: launch_t<WT, 2>(p, s); break;
@@ -463,6 +603,11 @@ void gemv_init_device() {
   set_attrs<W_BF16>();
   set_attrs<W_Q8>();
   set_attrs<W_Q4>();
+}
+
+int gemv_launches(const GemvParams& p) {
+  const int cap = max_nb(p);
+  return (p.nb + cap - 1) / cap;
 }
 
 void launch_gemv(const GemvParams& p, cudaStream_t s) {

@@ -7,9 +7,11 @@
 namespace svl {
 
 // CTAs of a logits product: the argmax scratch holds one (value, index) pair per CTA.
-constexpr int kLogitsGrid = 148;
+constexpr int kLogitsGrid = 296;
 // Streams one product launch covers at most (the argmax scratch is [kMaxNbChunk][kLogitsGrid]).
 constexpr int kMaxNbChunk = 8;
+// Audio codebooks the embedding kernel stages per stream.
+constexpr int kMaxCodebooks = 127;
 
 enum GemvEpilogue {
   EPI_STORE = 0,     // out = acc (+ bias)
@@ -22,7 +24,9 @@ enum GemvEpilogue {
   EPI_SILU = 7       // out = silu(acc (+ bias))
 };
 
-// One matrix-vector product over `nb` streams: out[b] = epilogue(W · norm(x[b])).
+// One matrix-vector product over `nb` streams: out[b] = epilogue(W · norm(x[b])). Every CTA
+// normalises and converts the input rows itself (see gemv.cu), while its first weight loads
+// are in flight.
 struct GemvParams {
   const uint8_t* w;      // device weights in the packed layout of `wtype`
   int64_t row_stride;    // bytes between rows
@@ -55,9 +59,15 @@ struct GemvParams {
   int* am_idx;           // [nb][grid] scratch
   unsigned* am_ticket;   // one counter, zero between launches
   uint32_t* tokens;      // [nb] argmax out
+  int* pos_advance;      // [nb] positions to advance once the argmax is final, or null
+  // L2 prefetch of a later kernel's weights: each CTA prefetches its share of [pf, pf+pf_bytes).
+  const uint8_t* pf;
+  int64_t pf_bytes;
 };
 
 void launch_gemv(const GemvParams& p, cudaStream_t s);
+// Kernel launches one launch_gemv(p) issues (streams are split into chunks that fit).
+int gemv_launches(const GemvParams& p);
 // Per device, once: raises the dynamic shared-memory limit of every product kernel.
 void gemv_init_device();
 
@@ -77,6 +87,7 @@ struct AttnParams {
 };
 
 void launch_attention_decode(const AttnParams& p, cudaStream_t s);
+int attention_max_splits();
 
 struct EmbedParams {
   const void* text_table;   // [text_card + 1][d]

@@ -6,19 +6,28 @@ namespace svl {
 namespace {
 
 // LanguageModel::step's input (stt/model.rs:246-250): the text embedding row, then each of
-// the n_q audio embedding rows added in codebook order, in f32. Same order and rounding as
-// the reference, so the sum is bit-identical to it.
+// the n_q audio embedding rows added in codebook order, in f32 -- the reference's order and
+// rounding, so the sum is bit-identical to it. One CTA per stream: the token ids are staged
+// first (validated; an id past its table sets the error flag and reads row 0), then every
+// thread sums its columns over the 1 + n_q rows.
 template <bool BF16>
-__global__ void embed_kernel(const EmbedParams p) {
-  const int b = blockIdx.y;
-  const int c4 = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c4 * 4 >= p.d) return;
-  uint32_t tt = p.text_tok[b];
-  if (tt > (uint32_t)p.text_card) {
-    atomicExch(p.error_flag, 1);
-    tt = 0;
+__global__ void __launch_bounds__(256) embed_kernel(const EmbedParams p) {
+  __shared__ uint32_t toks[kMaxCodebooks + 1];
+  const int b = blockIdx.x, t = threadIdx.x;
+  // x is still read by the previous kernel (programmatic dependent launch).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (t <= p.n_q) {
+    uint32_t v = t == 0 ? p.text_tok[b] : p.audio_tok[b * p.n_q + t - 1];
+    const uint32_t lim = t == 0 ? (uint32_t)p.text_card : (uint32_t)p.card;
+    if (v > lim) {
+      atomicExch(p.error_flag, 1);
+      v = 0;
+    }
+    toks[t] = v;
   }
-  auto row = [&](const void* table, int64_t r) -> float4 {
+  __syncthreads();
+  auto row = [&](const void* table, int64_t r, int c4) -> float4 {
     if (BF16) {
       const uint2 v = reinterpret_cast<const uint2*>(
           reinterpret_cast<const __nv_bfloat16*>(table) + r * p.d)[c4];
@@ -26,20 +35,19 @@ __global__ void embed_kernel(const EmbedParams p) {
     }
     return reinterpret_cast<const float4*>(reinterpret_cast<const float*>(table) + r * p.d)[c4];
   };
-  float4 acc = row(p.text_table, tt);
-  for (int c = 0; c < p.n_q; c++) {
-    uint32_t a = p.audio_tok[b * p.n_q + c];
-    if (a > (uint32_t)p.card) {
-      atomicExch(p.error_flag, 1);
-      a = 0;
+  float* x = p.x + (int64_t)b * p.d;
+  for (int c4 = t; c4 < p.d / 4; c4 += 256) {
+    float4 acc = row(p.text_table, toks[0], c4);
+#pragma unroll 8
+    for (int c = 0; c < p.n_q; c++) {
+      const float4 e = row(p.audio_tables, (int64_t)c * (p.card + 1) + toks[c + 1], c4);
+      acc.x = acc.x + e.x;
+      acc.y = acc.y + e.y;
+      acc.z = acc.z + e.z;
+      acc.w = acc.w + e.w;
     }
-    float4 e = row(p.audio_tables, (int64_t)c * (p.card + 1) + a);
-    acc.x = acc.x + e.x;
-    acc.y = acc.y + e.y;
-    acc.z = acc.z + e.z;
-    acc.w = acc.w + e.w;
+    reinterpret_cast<float4*>(x)[c4] = acc;
   }
-  reinterpret_cast<float4*>(p.x + (int64_t)b * p.d)[c4] = acc;
 }
 
 __global__ void advance_kernel(int* pos, int nb) {
@@ -106,11 +114,19 @@ __global__ void round_bf16_kernel(float* p, int64_t n) {
 }  // namespace
 
 void launch_embed(const EmbedParams& p, cudaStream_t s) {
-  dim3 grid((p.d / 4 + 127) / 128, p.nb);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.nb);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (p.tables_bf16)
-    embed_kernel<true><<<grid, 128, 0, s>>>(p);
+    cudaLaunchKernelEx(&cfg, embed_kernel<true>, p);
   else
-    embed_kernel<false><<<grid, 128, 0, s>>>(p);
+    cudaLaunchKernelEx(&cfg, embed_kernel<false>, p);
 }
 
 void launch_advance_positions(int* pos, int nb, cudaStream_t s) {
