@@ -224,6 +224,7 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
   if (device < 0 || device >= count) throw Error(SVL_ERR_CUDA, "no such CUDA device");
   check_cuda(cudaSetDevice(device), "cudaSetDevice");
   gemv_init_device();
+  attention_init_device();
   Model* m = new Model();
   try {
     m->kind = kind;
@@ -294,14 +295,12 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     s->q.alloc((int64_t)max_batch * qd * 4);
     s->attn.alloc((int64_t)max_batch * qd * 4);
     s->act.alloc((int64_t)max_batch * c.ffn_hidden * 4);
-    // Split the keys of a (stream, head) so that batch 1 still covers the SMs.
+    // Split the keys of a (stream, head) over a cluster of CTAs so that small batches still
+    // cover the SMs.
     const int units = max_batch * c.num_heads;
-    int splits = (2 * 148 + units - 1) / units;
-    splits = std::max(1, std::min({splits, (s->cap + 31) / 32, attention_max_splits()}));
+    int splits = (148 + units - 1) / units;
+    splits = std::max(1, std::min({splits, (s->cap + 15) / 16, attention_max_splits()}));
     s->splits = splits;
-    s->part.alloc((int64_t)max_batch * c.num_heads * splits * (c.head_dim + 2) * 4);
-    s->tickets.alloc((int64_t)max_batch * c.num_heads * 4);
-    check_cuda(cudaMemsetAsync(s->tickets.p, 0, s->tickets.bytes, m->stream), "memset");
     s->am_val.alloc(kMaxNbChunk * kLogitsGrid * 4);
     s->am_idx.alloc(kMaxNbChunk * kLogitsGrid * 4);
     s->am_ticket.alloc(4);
@@ -427,9 +426,8 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     a.window = c.context;
     a.scale = std::pow((float)hd, -0.5f);
     a.splits = s.splits;
-    a.part = s.part.as<float>();
-    a.tickets = s.tickets.as<unsigned>();
     a.out = attn;
+    a.err = s.err.as<int>();
     if (do_attn) launch_attention_decode(a, st);
     if (!do_lin) continue;
     // out_proj + residual (nn/transformer.rs:344, :239-243).

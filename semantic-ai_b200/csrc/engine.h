@@ -122,7 +122,7 @@ struct State {
   // work buffers
   DevBuf x, q, attn, act, logits, extra_logits, extra_p;
   DevBuf tok_in, audio_in, tok_out;
-  DevBuf am_val, am_idx, am_ticket, part, tickets, err;
+  DevBuf am_val, am_idx, am_ticket, err;
   DevBuf frames_audio, frames_out;  // svl_stt_run_frames
   // TTS work buffers
   DevBuf latent_in, noise, latent_out, eos, z, y, sy, hbuf, h2buf, modbuf, xs2, tmp;

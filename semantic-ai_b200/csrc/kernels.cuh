@@ -80,14 +80,15 @@ struct AttnParams {
   const int* pos;        // [nb] position of the newest key (already written)
   int nb, heads, kv_heads, head_dim, ring_cap, window;  // window 0 = unlimited
   float scale;
-  int splits;            // key chunks per (stream, head)
-  float* part;           // [nb][heads][splits][head_dim + 2] scratch
-  unsigned* tickets;     // [nb][heads], zero between launches
+  int splits;            // key chunks per (stream, head): one thread-block cluster
   float* out;            // [nb][heads * head_dim]
+  int* err;              // set to 1 when a bounded wait runs out
 };
 
 void launch_attention_decode(const AttnParams& p, cudaStream_t s);
 int attention_max_splits();
+// Per device, once: raises the dynamic shared-memory limit of the attention kernels.
+void attention_init_device();
 
 struct EmbedParams {
   const void* text_table;   // [text_card + 1][d]
