@@ -187,6 +187,25 @@ SVL_API svl_status svl_profile_kernels(svl_model* model, svl_state* state, int32
                                        int32_t which, int32_t iters, void* cuda_stream,
                                        int64_t* bytes_per_iter);
 
+/* The greedy head alone -- out_norm, text_linear and argmax, the end of LanguageModel::step
+ * -- for callers that cannot allocate device memory. It has no counterpart in the
+ * reference: it exists for hosts that own every device allocation of the process (a plugin
+ * host's memory pool, a real-time audio thread that must never enter the allocator, code
+ * where a cudaMalloc would synchronise the device mid-stream) and so cannot create a state,
+ * whose scratch svl_stt_step uses.
+ * d_hidden [batch][d_model] f32 (the transformer output), d_tokens [batch] out, d_logits
+ * [batch][text_card] out or NULL; device pointers, enqueued on cuda_stream (NULL = the
+ * model's stream). The argmax scratch is a fixed 19,200-byte __device__ array inside the
+ * library (every GPU that loads the library holds it until the process exits): batch is
+ * limited to 8 streams per call, larger batches are rejected with SVL_ERR_INVALID_INPUT.
+ * Nothing is allocated: the first call on a device looks up the array's device address
+ * (make that first call before any stream capture), every call clears the array's counter
+ * on the stream and launches the head. All calls share the array, so calls that overlap on
+ * the GPU (on different streams, or on different models of one device) race: serialise
+ * them. */
+SVL_API svl_status svl_stt_head_noalloc(svl_model* model, int32_t batch, const float* d_hidden,
+                                        uint32_t* d_tokens, float* d_logits, void* cuda_stream);
+
 /* Message of the last failure on this thread ("" when none). */
 SVL_API const char* svl_last_error(void);
 SVL_API const char* svl_version(void);

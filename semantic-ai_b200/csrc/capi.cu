@@ -7,14 +7,6 @@
 
 using svl::Error;
 
-struct svl_model {
-  svl::Model* m;
-};
-struct svl_state {
-  svl::State* s;
-  svl_model* model;
-};
-
 namespace {
 
 thread_local std::string g_err;
@@ -55,6 +47,8 @@ void check_room(svl::State& s, int nb, int steps) {
 }
 
 }  // namespace
+
+void svl::set_last_error(const std::string& msg) { g_err = msg; }
 
 extern "C" {
 

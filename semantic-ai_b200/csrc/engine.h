@@ -148,8 +148,19 @@ int64_t enqueue_profile(Model& m, State& s, int nb, int which, cudaStream_t st);
 void enqueue_tts_step(Model& m, State& s, int nb, int decode_steps, bool bos, cudaStream_t st);
 
 void state_reset(State& s, int stream);
+// Message of the last failure on this thread (svl_last_error).
+void set_last_error(const std::string& msg);
 void state_export(State& s, int stream, int layer, float* k, float* v, int* len);
 void state_import(State& s, int stream, int layer, const float* k, const float* v, int len,
                   int position);
 
 }  // namespace svl
+
+// The C ABI's opaque handles.
+struct svl_model {
+  svl::Model* m;
+};
+struct svl_state {
+  svl::State* s;
+  svl_model* model;
+};
