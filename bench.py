@@ -16,7 +16,6 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
-import math
 import os
 import subprocess
 import sys
@@ -107,26 +106,6 @@ class ClockSampler:
 
 def preset(name: str) -> C.SttConfig:
     return getattr(C, name)()
-
-
-def gemv_launches(cfg: C.TransformerConfig, stt: C.SttConfig, batch: int) -> int:
-    """Kernel launches of one step, as the engine issues them (launch_gemv splits the streams
-    into chunks whose input rows fit in 200 KB of shared memory)."""
-    wt = {"f32": 0, "bf16": 1, "q8_0": 2, "q4_1": 3}[cfg.weight_dtype]
-
-    def chunks(k, quantised=True):
-        t = wt if (quantised or wt == 1) else 0
-        for nb in (8, 4, 2, 1):
-            sm = nb * k * 4 if t in (0, 1) else nb * k + nb * (k // 32) * 4 * (2 if t == 3 else 1)
-            if sm <= 200 * 1024:
-                return math.ceil(batch / nb)
-        return batch
-
-    d, qd = cfg.d_model, cfg.num_heads * cfg.head_dim
-    per_layer = chunks(d) + 1 + chunks(qd) + chunks(d) + chunks(cfg.ffn_hidden)
-    n = 1 + cfg.num_layers * per_layer + chunks(d)
-    n += stt.extra_heads_num_heads * chunks(d, False) + (1 if stt.extra_heads_num_heads else 0)
-    return n + 1
 
 
 def run_ours(args, spec, rank, world, local_rank):
@@ -263,7 +242,11 @@ def run_ours(args, spec, rank, world, local_rank):
                       "gbs": nbytes.value / (per / 1e3) / 1e9}
     st.close()
     dom = max(kern, key=lambda k: kern[k]["ms_per_step"])
-    launches = gemv_launches(cfg, stt, B)
+    nk = ctypes.c_int32()
+    st = fresh_state()
+    _lib.check(L.svl_step_kernel_count(model.handle, st.handle, B, ctypes.byref(nk)))
+    st.close()
+    launches = nk.value
     n_launch_dom = (cfg.num_layers * 4 + 1) if dom.startswith("gemv") else cfg.num_layers
     traffic = None
     tfile = ROOT / "profiles" / f"traffic_config{args.config}.json"

@@ -187,6 +187,12 @@ SVL_API svl_status svl_profile_kernels(svl_model* model, svl_state* state, int32
                                        int32_t which, int32_t iters, void* cuda_stream,
                                        int64_t* bytes_per_iter);
 
+/* Kernels one svl_stt_step / svl_stt_step_device call launches at this batch size: the
+ * kernel nodes of the step's CUDA graph, which this call captures if no step of that batch
+ * size ran yet. Diagnostics only; no counterpart in the reference. */
+SVL_API svl_status svl_step_kernel_count(svl_model* model, svl_state* state, int32_t batch,
+                                         int32_t* kernels);
+
 /* The greedy head alone -- out_norm, text_linear and argmax, the end of LanguageModel::step
  * -- for callers that cannot allocate device memory. It has no counterpart in the
  * reference: it exists for hosts that own every device allocation of the process (a plugin

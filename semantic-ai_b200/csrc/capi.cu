@@ -355,6 +355,20 @@ SVL_API svl_status svl_profile_kernels(svl_model* model, svl_state* state, int32
   });
 }
 
+SVL_API svl_status svl_step_kernel_count(svl_model* model, svl_state* state, int32_t batch,
+                                         int32_t* kernels) {
+  return guarded([&] {
+    need(model && state && kernels, SVL_ERR_INVALID_INPUT, "null argument");
+    svl::Model& m = *model->m;
+    svl::State& s = *state->s;
+    need(m.kind == 0, SVL_ERR_INVALID_INPUT, "not an STT model");
+    need(s.m == &m, SVL_ERR_INVALID_INPUT, "state of another model");
+    need(batch >= 1 && batch <= s.max_batch, SVL_ERR_INVALID_INPUT, "batch out of range");
+    svl::check_cuda(cudaSetDevice(m.device), "cudaSetDevice");
+    *kernels = svl::capture_stt_graph(m, s, batch, m.stream);
+  });
+}
+
 SVL_API svl_status svl_tts_prompt_text(svl_model* model, svl_state* state, int32_t stream,
                                        const uint32_t* tokens, int32_t n) {
   return fail(SVL_ERR_UNSUPPORTED, "the Pocket-TTS step is not built yet");

@@ -126,6 +126,8 @@ struct Loader {
     float* src = stage(v);
     launch_pack_linear(src, L.w.as<uint8_t>(), L.row_stride, n_out, k, wt, interleave, m.stream);
     check_cuda(cudaStreamSynchronize(m.stream), "pack weights");
+    if (wt == W_BF16 && !make_gemm_operand(L.tc, L.w.p, n_out, k, L.row_stride, 128))
+      throw Error(SVL_ERR_CUDA, "linear " + wname + ": cannot encode its TMA tensor map");
     if (!bname.empty()) L.bias = vec(bname, n_out);
     m.weight_bytes += L.row_stride * n_out;
   }
@@ -224,6 +226,7 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
   if (device < 0 || device >= count) throw Error(SVL_ERR_CUDA, "no such CUDA device");
   check_cuda(cudaSetDevice(device), "cudaSetDevice");
   gemv_init_device();
+  gemm_init_device();
   attention_init_device();
   Model* m = new Model();
   try {
@@ -301,8 +304,29 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     int splits = (148 + units - 1) / units;
     splits = std::max(1, std::min({splits, (s->cap + 15) / 16, attention_max_splits()}));
     s->splits = splits;
-    s->am_val.alloc(kMaxNbChunk * kLogitsGrid * 4);
-    s->am_idx.alloc(kMaxNbChunk * kLogitsGrid * 4);
+    // Argmax candidates: [stream][CTA] of the matrix-vector head, [stream][row tile] of the
+    // tensor-core head.
+    int64_t cand = kMaxNbChunk * kLogitsGrid;
+    if (m->kind == 0) cand = std::max<int64_t>(cand, (int64_t)max_batch * ((m->stt.text_card + 127) / 128));
+    s->am_val.alloc(cand * 4);
+    s->am_idx.alloc(cand * 4);
+    if (c.weight_dtype == SVL_DT_BF16 && max_batch >= kGemmMinBatch) {
+      const int kx = std::max(d, qd);
+      s->xa.alloc((int64_t)max_batch * kx * 2);
+      s->xh.alloc((int64_t)max_batch * c.ffn_hidden * 2);
+      check_cuda(cudaMemsetAsync(s->xa.p, 0, s->xa.bytes, m->stream), "memset");
+      check_cuda(cudaMemsetAsync(s->xh.p, 0, s->xh.bytes, m->stream), "memset");
+      s->rope_cs.alloc((int64_t)max_batch * (c.head_dim / 2) * 8);
+      s->gemm_ws.alloc(gemm_workspace_bytes());
+      const int bns[3] = {64, 128, 256};
+      for (int i = 0; i < 3; i++) {
+        bool ok = make_gemm_operand(s->xa_d[i], s->xa.p, max_batch, d, (int64_t)d * 2, bns[i]) &&
+                  make_gemm_operand(s->xa_q[i], s->xa.p, max_batch, qd, (int64_t)qd * 2, bns[i]) &&
+                  make_gemm_operand(s->xh_f[i], s->xh.p, max_batch, c.ffn_hidden,
+                                    (int64_t)c.ffn_hidden * 2, bns[i]);
+        if (!ok) throw Error(SVL_ERR_CUDA, "cannot encode the TMA tensor maps of the GEMM operands");
+      }
+    }
     s->am_ticket.alloc(4);
     check_cuda(cudaMemsetAsync(s->am_ticket.p, 0, 4, m->stream), "memset");
     s->err.alloc(4);
@@ -374,6 +398,17 @@ void set_prefetch(GemvParams& g, const Model& m, int l, const Linear& (*pick)(co
 void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bool do_lin,
                          bool do_attn);
 
+bool use_tensor_cores(const Model& m, const State& s, int nb) {
+  return m.cfg.weight_dtype == SVL_DT_BF16 && nb >= kGemmMinBatch && s.xa.p != nullptr;
+}
+
+namespace {
+int tile_index(int nb) {
+  const int bn = gemm_stream_tile(nb);
+  return bn == 64 ? 0 : bn == 128 ? 1 : 2;
+}
+}  // namespace
+
 void enqueue_layers(Model& m, State& s, int b0, int nb, cudaStream_t st) {
   enqueue_layers_mask(m, s, b0, nb, st, true, true);
 }
@@ -387,6 +422,10 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
   float* attn = s.attn.as<float>() + (int64_t)b0 * qd;
   float* act = s.act.as<float>() + (int64_t)b0 * c.ffn_hidden;
   const int* pos = s.pos.as<int>() + b0;
+  const bool tc = use_tensor_cores(m, s, nb);
+  const int ti = tc ? tile_index(nb) : 0;
+  float2* rope_cs = tc ? s.rope_cs.as<float2>() + (int64_t)b0 * (hd / 2) : nullptr;
+  if (tc && do_lin) launch_rope_table(pos, nb, m.inv_freq.as<float>(), hd / 2, rope_cs, st);
   for (int l = 0; l < c.num_layers; l++) {
     const Layer& L = m.layers[l];
     uint8_t* kr = s.k_ring.as<uint8_t>() + ((int64_t)l * s.ring_layer_stride + (int64_t)b0 * s.ring_stream_stride) * s.kv_elt;
@@ -398,6 +437,7 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g.out = q;
     g.out_stride = qd;
     g.inv_freq = m.inv_freq.as<float>();
+    g.rope_cs = rope_cs;
     g.pos = pos;
     g.q_dim = qd;
     g.kv_dim = kvd;
@@ -409,7 +449,13 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g.ring_stream_stride = s.ring_stream_stride;
     g.kv_bf16 = s.kv_elt == 2;
     set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.in_proj; });
-    if (do_lin) launch_gemv(g, st);
+    if (do_lin && tc) {
+      launch_prep_bf16(x, d, nb, L.norm1.kind, L.norm1.w.as<float>(), L.norm1.b.as<float>(),
+                       L.norm1.eps, d, s.xa.p, d, st);
+      launch_gemm(g, L.in_proj.tc, s.xa_d[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
+    } else if (do_lin) {
+      launch_gemv(g, st);
+    }
     // Sliding-window attention (nn/kernels/attention.rs:81-169).
     AttnParams a{};
     a.q = q;
@@ -437,7 +483,12 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g.out_stride = d;
     g.ls = L.ls1.as<float>();
     set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.out_proj; });
-    launch_gemv(g, st);
+    if (tc) {
+      launch_prep_bf16(attn, qd, nb, NORM_NONE, nullptr, nullptr, 0.f, qd, s.xa.p, qd, st);
+      launch_gemm(g, L.out_proj.tc, s.xa_q[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
+    } else {
+      launch_gemv(g, st);
+    }
     // norm2 + feed-forward (nn/transformer.rs:438-464).
     g = gemv_base(L.ff1, x, d, nb);
     set_norm(g, L.norm2);
@@ -446,14 +497,24 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g.epi = c.ffn_kind == SVL_FFN_GATED_SILU ? EPI_SWIGLU
             : c.ffn_kind == SVL_FFN_PLAIN_GELU_ERF ? EPI_GELU_ERF : EPI_GELU_TANH;
     set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.ff1; });
-    launch_gemv(g, st);
+    if (tc) {
+      launch_prep_bf16(x, d, nb, L.norm2.kind, L.norm2.w.as<float>(), L.norm2.b.as<float>(),
+                       L.norm2.eps, d, s.xa.p, d, st);
+      g.out = s.xh.as<float>();  // bf16 hidden rows, the operand of linear_out
+      launch_gemm(g, L.ff1.tc, s.xa_d[ti], 0, 1, s.err.as<int>(), s.gemm_ws.as<float>(), st);
+    } else {
+      launch_gemv(g, st);
+    }
     g = gemv_base(L.ff2, act, c.ffn_hidden, nb);
     g.epi = EPI_RESIDUAL;
     g.out = x;
     g.out_stride = d;
     g.ls = L.ls2.as<float>();
     set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.ff2; });
-    launch_gemv(g, st);
+    if (tc)
+      launch_gemm(g, L.ff2.tc, s.xh_f[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
+    else
+      launch_gemv(g, st);
   }
 }
 
@@ -477,6 +538,19 @@ GemvParams head_params(Model& m, State& s, int nb) {
 
 }  // namespace
 
+// The logits product with its argmax: on the tensor cores (out_norm as the operand prep)
+// when the step's products run there.
+void launch_head(Model& m, State& s, const GemvParams& g, cudaStream_t st) {
+  if (use_tensor_cores(m, s, g.nb)) {
+    const int d = m.cfg.d_model;
+    launch_prep_bf16(g.x, d, g.nb, m.out_norm.kind, m.out_norm.w.as<float>(),
+                     m.out_norm.b.as<float>(), m.out_norm.eps, d, s.xa.p, d, st);
+    launch_gemm(g, m.text_linear.tc, s.xa_d[tile_index(g.nb)], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
+  } else {
+    launch_gemv(g, st);
+  }
+}
+
 void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
   const auto& c = m.cfg;
   const int d = c.d_model;
@@ -499,7 +573,7 @@ void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
   // positions is done once the argmax is final: the argmax's last CTA advances them.
   GemvParams g = head_params(m, s, nb);
   g.pos_advance = s.pos.as<int>();
-  launch_gemv(g, st);
+  launch_head(m, s, g, st);
   // Extra (VAD) heads: softmax p[0] of each (stt/model.rs:259-271); never quantised.
   const int eh = m.stt.extra_heads_num, edim = m.stt.extra_heads_dim;
   for (int i = 0; i < eh; i++) {
@@ -513,33 +587,51 @@ void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
   if (eh > 0) launch_extra_heads(s.extra_logits.as<float>(), nb, eh, edim, s.extra_p.as<float>(), st);
 }
 
-void launch_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
+int capture_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
   auto it = s.graphs.find(nb);
-  if (it == s.graphs.end()) {
-    cudaGraph_t graph = nullptr;
-    check_cuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture");
-    try {
-      enqueue_stt_step(m, s, nb, st);
-    } catch (...) {
-      cudaStreamEndCapture(st, &graph);
-      if (graph) cudaGraphDestroy(graph);
-      throw;
-    }
-    check_cuda(cudaStreamEndCapture(st, &graph), "end capture");
-    cudaGraphExec_t exec = nullptr;
-    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    check_cuda(e, "graph instantiate");
-    it = s.graphs.emplace(nb, exec).first;
+  if (it != s.graphs.end()) return s.graph_kernels[nb];
+  cudaGraph_t graph = nullptr;
+  check_cuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture");
+  try {
+    enqueue_stt_step(m, s, nb, st);
+  } catch (...) {
+    cudaStreamEndCapture(st, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    throw;
   }
-  check_cuda(cudaGraphLaunch(it->second, st), "graph launch");
+  check_cuda(cudaStreamEndCapture(st, &graph), "end capture");
+  // Count the kernel nodes: the launches one replay of the step makes.
+  size_t n = 0;
+  int kernels = 0;
+  cudaError_t e = cudaGraphGetNodes(graph, nullptr, &n);
+  if (e == cudaSuccess && n) {
+    std::vector<cudaGraphNode_t> nodes(n);
+    e = cudaGraphGetNodes(graph, nodes.data(), &n);
+    for (size_t i = 0; e == cudaSuccess && i < n; i++) {
+      cudaGraphNodeType t;
+      e = cudaGraphNodeGetType(nodes[i], &t);
+      if (e == cudaSuccess && t == cudaGraphNodeTypeKernel) kernels++;
+    }
+  }
+  cudaGraphExec_t exec = nullptr;
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  check_cuda(e, "graph instantiate");
+  s.graphs.emplace(nb, exec);
+  s.graph_kernels[nb] = kernels;
+  return kernels;
+}
+
+void launch_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
+  capture_stt_graph(m, s, nb, st);
+  check_cuda(cudaGraphLaunch(s.graphs[nb], st), "graph launch");
 }
 
 int64_t enqueue_profile(Model& m, State& s, int nb, int which, cudaStream_t st) {
   const auto& c = m.cfg;
   if (which == 0) {
     enqueue_layers_mask(m, s, 0, nb, st, true, false);
-    launch_gemv(head_params(m, s, nb), st);
+    launch_head(m, s, head_params(m, s, nb), st);
     int64_t bytes = m.text_linear.bytes();
     for (const Layer& L : m.layers)
       bytes += L.in_proj.bytes() + L.out_proj.bytes() + L.ff1.bytes() + L.ff2.bytes();

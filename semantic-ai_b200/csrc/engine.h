@@ -58,6 +58,7 @@ struct Linear {
   int interleave = 0;
   DevBuf w;
   DevBuf bias;  // f32 [n] or empty
+  GemmOperand tc;  // TMA map of w for the tensor-core path (bf16 weights)
   int64_t bytes() const { return row_stride * n + (bias.p ? 4LL * n : 0); }
 };
 
@@ -128,9 +129,20 @@ struct State {
   DevBuf latent_in, noise, latent_out, eos, z, y, sy, hbuf, h2buf, modbuf, xs2, tmp;
   HostBuf h_tok_in, h_audio_in, h_tok_out;
   int splits = 1;
+  // Tensor-core path (bf16 weights, many streams): bf16 operand rows and their TMA maps, per
+  // stream-tile width (64, 128, 256). xa holds normalised inputs / attention outputs, xh the
+  // feed-forward hidden rows.
+  DevBuf xa, xh, gemm_ws;
+  DevBuf rope_cs;  // [max_batch][head_dim / 2] float2, refreshed at the start of every forward
+  GemmOperand xa_d[3], xa_q[3], xh_f[3];
   std::map<int, cudaGraphExec_t> graphs;
+  std::map<int, int> graph_kernels;  // kernel nodes of each captured step graph
   ~State();
 };
+
+// Streams from which a step's weight products run on the tensor cores (bf16 weights).
+constexpr int kGemmMinBatch = 16;
+bool use_tensor_cores(const Model& m, const State& s, int nb);
 
 // Weight loading (LanguageModel::new / FlowLm::new).
 Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_config* stt,
@@ -143,6 +155,8 @@ void enqueue_layers(Model& m, State& s, int b0, int nb, cudaStream_t st);
 void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st);
 // Runs the captured graph of the STT step for nb streams (captures it on first use).
 void launch_stt_graph(Model& m, State& s, int nb, cudaStream_t st);
+// Captures the step graph of batch size nb if it is not captured yet; returns its kernels.
+int capture_stt_graph(Model& m, State& s, int nb, cudaStream_t st);
 // Profiling: one repetition of the step's weight products (which 0) or attention (which 1).
 int64_t enqueue_profile(Model& m, State& s, int nb, int which, cudaStream_t st);
 void enqueue_tts_step(Model& m, State& s, int nb, int decode_steps, bool bos, cudaStream_t st);

@@ -46,6 +46,7 @@ struct GemvParams {
   const float* ls;       // layer scale [n] or null (EPI_RESIDUAL)
   // EPI_QKV_ROPE
   const float* inv_freq; // [head_dim / 2]
+  const float2* rope_cs; // [nb][head_dim / 2] (cos, sin) of pos * inv_freq (tensor-core path)
   const int* pos;        // [nb] absolute positions of the new token
   int q_dim, kv_dim, head_dim;
   int ring_cap;          // KV slots per stream and head
@@ -70,6 +71,32 @@ void launch_gemv(const GemvParams& p, cudaStream_t s);
 int gemv_launches(const GemvParams& p);
 // Per device, once: raises the dynamic shared-memory limit of every product kernel.
 void gemv_init_device();
+
+// A bf16 GEMM operand in global memory: rows of k elements, row_bytes apart, described by a
+// TMA tensor map whose box is 64 elements (128 bytes, 128-byte swizzle) by box_rows rows.
+struct GemmOperand {
+  alignas(64) unsigned char map[128];  // CUtensorMap
+  int rows = 0, k = 0, box_rows = 0;
+  bool valid = false;
+};
+bool make_gemm_operand(GemmOperand& op, const void* base, int rows, int k, int64_t row_bytes,
+                       int box_rows);
+// Streams per GEMM tile (the MMA's N, and the box height of the X operand) for nb streams.
+int gemm_stream_tile(int nb);
+// Cluster split of K for an n x k product over nb streams with stream tiles of bn.
+int gemm_split(int n, int k, int nb, int bn);
+// out[b] = epilogue(W . X[x_row0 + b]) for b < p.nb on the tensor cores; p gives the sizes
+// and the epilogue (p.x / p.norm are not read: X is the bf16 operand). out_bf16 writes the
+// STORE / SWIGLU / GELU / SILU outputs as bf16. err is set to 2 if a bounded wait ran out.
+// ws: the split-K exchange, gemm_workspace_bytes() of device memory.
+void launch_gemm(const GemvParams& p, const GemmOperand& w, const GemmOperand& x, int x_row0,
+                 int out_bf16, int* err, float* ws, cudaStream_t s);
+size_t gemm_workspace_bytes();
+// The norm of each of nb rows of x (NormKind), as bf16 rows of the GEMM operand.
+void launch_prep_bf16(const float* x, int64_t x_stride, int nb, int norm, const float* norm_w,
+                      const float* norm_b, float eps, int k, void* out, int64_t out_stride,
+                      cudaStream_t s);
+void gemm_init_device();
 
 struct AttnParams {
   const float* q;        // [nb][heads][head_dim] (after RoPE)
@@ -103,6 +130,10 @@ struct EmbedParams {
 
 void launch_embed(const EmbedParams& p, cudaStream_t s);
 void launch_advance_positions(int* pos, int nb, cudaStream_t s);
+// cs[b][i] = (cos, sin)(pos[b] * inv_freq[i]) for the streams' new tokens: one evaluation per
+// (stream, frequency) per step, shared by every layer's RoPE epilogue.
+void launch_rope_table(const int* pos, int nb, const float* inv_freq, int half, float2* cs,
+                       cudaStream_t s);
 
 // Weight packing: f32 [n][k] (device) into the layout of wtype. interleave_half = F swaps
 // rows so that packed row 2i is source row i and 2i+1 is source row F + i (SwiGLU).

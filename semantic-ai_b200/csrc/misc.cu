@@ -1,6 +1,7 @@
 // misc.cu — embedding sum, position advance and weight packing.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "sm100.cuh"
 
 namespace svl {
 namespace {
@@ -127,6 +128,32 @@ void launch_embed(const EmbedParams& p, cudaStream_t s) {
     cudaLaunchKernelEx(&cfg, embed_kernel<true>, p);
   else
     cudaLaunchKernelEx(&cfg, embed_kernel<false>, p);
+}
+
+__global__ void rope_table_kernel(const int* pos, int nb, const float* inv_freq, int half, float2* cs) {
+  pdl_launch();
+  pdl_wait();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)nb * half) return;
+  const int b = (int)(i / half), f = (int)(i % half);
+  float sn, c;
+  sincosf((float)pos[b] * inv_freq[f], &sn, &c);
+  cs[i] = make_float2(c, sn);
+}
+
+void launch_rope_table(const int* pos, int nb, const float* inv_freq, int half, float2* cs,
+                       cudaStream_t s) {
+  const int64_t n = (int64_t)nb * half;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((n + 255) / 256));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, rope_table_kernel, pos, nb, inv_freq, half, cs);
 }
 
 void launch_advance_positions(int* pos, int nb, cudaStream_t s) {

@@ -45,10 +45,12 @@ class State:
         self.handle = h
         self.model = model
         self.max_batch = max_batch
+        # Bound now: at interpreter exit the module globals may already be gone.
+        self._destroy = _lib.lib().svl_state_destroy
 
     def close(self):
         if self.handle:
-            _lib.lib().svl_state_destroy(self.handle)
+            self._destroy(self.handle)
             self.handle = None
 
     __del__ = close
@@ -92,9 +94,11 @@ class _Model:
     handle = None
     max_positions_hint = 0
 
+    _destroy = None
+
     def close(self):
         if self.handle:
-            _lib.lib().svl_model_destroy(self.handle)
+            (self._destroy or _lib.lib().svl_model_destroy)(self.handle)
             self.handle = None
 
     __del__ = close
@@ -127,6 +131,7 @@ class LanguageModel(_Model):
         _lib.check(_lib.lib().svl_stt_model_create(ctypes.byref(c), ctypes.byref(s), views,
                                                    len(tensors), device, ctypes.byref(h)))
         self.handle = h
+        self._destroy = _lib.lib().svl_model_destroy
         del keep
 
     def step(self, text_tokens, audio_tokens, state: State, logits: bool = False,
@@ -172,6 +177,7 @@ class FlowLm(_Model):
         _lib.check(_lib.lib().svl_tts_model_create(ctypes.byref(c), ctypes.byref(t), views,
                                                    len(tensors), device, ctypes.byref(h)))
         self.handle = h
+        self._destroy = _lib.lib().svl_model_destroy
         del keep
 
     def prompt_text(self, tokens, state: State, stream: int = 0):
