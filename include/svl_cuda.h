@@ -169,6 +169,11 @@ SVL_API svl_status svl_transformer_forward(svl_model* model, svl_state* state, i
 SVL_API svl_status svl_tts_prompt_text(svl_model* model, svl_state* state, int32_t stream,
                                        const uint32_t* tokens, int32_t n);
 
+/* FlowLm::prompt_text (tts/flow_lm.rs:150-158) for streams 0..batch-1 at once, n tokens
+ * each: tokens [batch][n]. */
+SVL_API svl_status svl_tts_prompt_text_batch(svl_model* model, svl_state* state, int32_t batch,
+                                             const uint32_t* tokens, int32_t n);
+
 /* FlowLm::step (tts/flow_lm.rs:162-185) for streams 0..batch-1: latent_in [batch][latent]
  * (NULL = BOS for every stream), noise [batch][latent] (the reference samples it on the host,
  * flow_lm.rs:187-203), latent_out [batch][latent], eos_logit [batch]. */

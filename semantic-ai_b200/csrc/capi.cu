@@ -369,15 +369,89 @@ SVL_API svl_status svl_step_kernel_count(svl_model* model, svl_state* state, int
   });
 }
 
+namespace {
+
+// FlowLm::prompt_text for streams [b0, b0 + nb), n tokens each (host tokens [nb][n]).
+void tts_prompt(svl::Model& m, svl::State& s, int b0, int nb, const uint32_t* tokens, int n) {
+  need(m.kind == 1, SVL_ERR_INVALID_INPUT, "not a TTS model");
+  need(tokens && n >= 1, SVL_ERR_INVALID_INPUT, "no tokens");
+  for (int64_t i = 0; i < (int64_t)nb * n; i++)
+    if (tokens[i] > (uint32_t)m.tts.text_bins)
+      throw Error(SVL_ERR_INVALID_INPUT, "text token " + std::to_string(tokens[i]) + " out of range");
+  for (int b = b0; b < b0 + nb; b++)
+    if (!s.windowed && s.hpos[b] + n > s.cap)
+      throw Error(SVL_ERR_INVALID_INPUT, "stream would exceed the state's max_positions");
+  svl::check_cuda(cudaSetDevice(m.device), "cudaSetDevice");
+  cudaStream_t st = m.stream;
+  const size_t bytes = (size_t)nb * n * 4;
+  if (s.prompt_tok.bytes < bytes) {
+    svl::check_cuda(cudaStreamSynchronize(st), "sync");
+    s.prompt_tok.alloc(bytes);
+  }
+  svl::check_cuda(cudaMemcpyAsync(s.prompt_tok.p, tokens, bytes, cudaMemcpyHostToDevice, st), "h2d");
+  svl::enqueue_tts_prompt(m, s, b0, nb, s.prompt_tok.as<uint32_t>(), n, st);
+  svl::check_cuda(cudaStreamSynchronize(st), "prompt");
+  for (int b = b0; b < b0 + nb; b++) s.hpos[b] += n;
+}
+
+}  // namespace
+
 SVL_API svl_status svl_tts_prompt_text(svl_model* model, svl_state* state, int32_t stream,
                                        const uint32_t* tokens, int32_t n) {
-  return fail(SVL_ERR_UNSUPPORTED, "the Pocket-TTS step is not built yet");
+  return guarded([&] {
+    need(model && state, SVL_ERR_INVALID_INPUT, "null argument");
+    svl::State& s = *state->s;
+    need(s.m == model->m, SVL_ERR_INVALID_INPUT, "state of another model");
+    check_stream(s, stream);
+    tts_prompt(*model->m, s, stream, 1, tokens, n);
+  });
+}
+
+SVL_API svl_status svl_tts_prompt_text_batch(svl_model* model, svl_state* state, int32_t batch,
+                                             const uint32_t* tokens, int32_t n) {
+  return guarded([&] {
+    need(model && state, SVL_ERR_INVALID_INPUT, "null argument");
+    svl::State& s = *state->s;
+    need(s.m == model->m, SVL_ERR_INVALID_INPUT, "state of another model");
+    need(batch >= 1 && batch <= s.max_batch, SVL_ERR_INVALID_INPUT, "batch out of range");
+    tts_prompt(*model->m, s, 0, batch, tokens, n);
+  });
 }
 
 SVL_API svl_status svl_tts_step(svl_model* model, svl_state* state, int32_t batch,
                                 const float* latent_in, const float* noise, int32_t decode_steps,
                                 float* latent_out, float* eos_logit) {
-  return fail(SVL_ERR_UNSUPPORTED, "the Pocket-TTS step is not built yet");
+  return guarded([&] {
+    need(model && state && noise && latent_out && eos_logit, SVL_ERR_INVALID_INPUT, "null argument");
+    svl::Model& m = *model->m;
+    svl::State& s = *state->s;
+    need(m.kind == 1, SVL_ERR_INVALID_INPUT, "not a TTS model");
+    need(s.m == &m, SVL_ERR_INVALID_INPUT, "state of another model");
+    need(batch >= 1 && batch <= s.max_batch, SVL_ERR_INVALID_INPUT, "batch out of range");
+    const int steps = decode_steps < 1 ? 1 : decode_steps;  // FlowHead::decode runs >= 1 step
+    need(steps <= 64, SVL_ERR_INVALID_INPUT, "decode_steps above 64");
+    for (int b = 0; b < batch; b++)
+      if (!s.windowed && s.hpos[b] + 1 > s.cap)
+        throw Error(SVL_ERR_INVALID_INPUT, "stream would exceed the state's max_positions");
+    svl::check_cuda(cudaSetDevice(m.device), "cudaSetDevice");
+    cudaStream_t st = m.stream;
+    const int lat = m.tts.latent_dim;
+    const size_t row = (size_t)lat * 4;
+    if (latent_in) {
+      svl::check_cuda(cudaMemcpyAsync(s.latent_in.p, latent_in, row * batch, cudaMemcpyHostToDevice, st), "h2d");
+    } else {
+      // BOS for every stream (FlowLm::step with previous = None, flow_lm.rs:167-170).
+      for (int b = 0; b < batch; b++)
+        svl::check_cuda(cudaMemcpyAsync(s.latent_in.as<uint8_t>() + row * b, m.bos.p, row,
+                                        cudaMemcpyDeviceToDevice, st), "bos");
+    }
+    svl::check_cuda(cudaMemcpyAsync(s.noise.p, noise, row * batch, cudaMemcpyHostToDevice, st), "h2d");
+    svl::launch_tts_graph(m, s, batch, steps, st);
+    svl::check_cuda(cudaMemcpyAsync(latent_out, s.latent_out.p, row * batch, cudaMemcpyDeviceToHost, st), "d2h");
+    svl::check_cuda(cudaMemcpyAsync(eos_logit, s.eos.p, (size_t)batch * 4, cudaMemcpyDeviceToHost, st), "d2h");
+    svl::check_cuda(cudaStreamSynchronize(st), "tts step");
+    for (int b = 0; b < batch; b++) s.hpos[b] += 1;
+  });
 }
 
 }  // extern "C"

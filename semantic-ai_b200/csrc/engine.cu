@@ -261,7 +261,52 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
         ld.linear(m->extra[i], "extra_heads." + std::to_string(i) + ".weight", "",
                   stt->extra_heads_dim, d, false);
     } else {
-      throw Error(SVL_ERR_UNSUPPORTED, "the Pocket-TTS step is not built yet");
+      // FlowLm::new (tts/flow_lm.rs:45-126), english config: no z_proj, no low-rank table.
+      if (!tts) throw Error(SVL_ERR_CONFIG, "missing TTS config");
+      m->tts = *tts;
+      const int lat = tts->latent_dim, dim = tts->flow_dim;
+      if (lat <= 0 || lat % 32 || dim <= 0 || dim % 32 || dim > 1024 || tts->flow_depth < 0 ||
+          tts->text_bins <= 0 || tts->flow_kind < 0 || tts->flow_kind > 3)
+        throw Error(SVL_ERR_CONFIG, "invalid TTS config");
+      m->cond_table = ld.vec("conditioner.embed.weight", (int64_t)(tts->text_bins + 1) * d);
+      ld.linear(m->input_linear, "input_linear.weight", "", d, lat, true);
+      ld.transformer("transformer.");
+      m->out_norm.kind = NORM_LAYER;
+      m->out_norm.eps = 1e-5f;
+      m->out_norm.w = ld.vec("out_norm.weight", d);
+      m->out_norm.b = ld.vec("out_norm.bias", d);
+      m->eos_w = ld.vec("out_eos.weight", d);
+      m->eos_b = ld.vec("out_eos.bias", 1);
+      m->bos = ld.vec("bos_emb", lat);
+      // FlowHead::new (tts/flow_lm.rs:239-257).
+      const int n_time = tts->flow_kind == 0 ? 2 : tts->flow_kind == 1 ? 1 : 0;
+      m->time_emb.resize(n_time);
+      for (int i = 0; i < n_time; i++) {
+        TimeEmbed& e = m->time_emb[i];
+        const std::string p = "flow_net.time_embed." + std::to_string(i) + ".";
+        e.freqs = ld.vec(p + "freqs", 128);
+        ld.linear(e.l1, p + "mlp.0.weight", p + "mlp.0.bias", dim, 256, false);
+        ld.linear(e.l2, p + "mlp.2.weight", p + "mlp.2.bias", dim, dim, false);
+        e.alpha = ld.vec(p + "mlp.3.alpha", dim);
+      }
+      ld.linear(m->cond_embed, "flow_net.cond_embed.weight", "flow_net.cond_embed.bias", dim, d, true);
+      ld.linear(m->input_proj, "flow_net.input_proj.weight", "flow_net.input_proj.bias", dim, lat, true);
+      m->res.resize(tts->flow_depth);
+      for (int i = 0; i < tts->flow_depth; i++) {
+        ResBlock& r = m->res[i];
+        const std::string p = "flow_net.res_blocks." + std::to_string(i) + ".";
+        r.ln.kind = NORM_LAYER;
+        r.ln.eps = 1e-6f;
+        r.ln.w = ld.vec(p + "in_ln.weight", dim);
+        r.ln.b = ld.vec(p + "in_ln.bias", dim);
+        ld.linear(r.mlp1, p + "mlp.0.weight", p + "mlp.0.bias", dim, dim, true);
+        ld.linear(r.mlp2, p + "mlp.2.weight", p + "mlp.2.bias", dim, dim, true);
+        ld.linear(r.mod, p + "adaLN_modulation.1.weight", p + "adaLN_modulation.1.bias", 3 * dim, dim, true);
+      }
+      ld.linear(m->final_mod, "flow_net.final_layer.adaLN_modulation.1.weight",
+                "flow_net.final_layer.adaLN_modulation.1.bias", 2 * dim, dim, true);
+      ld.linear(m->final_linear, "flow_net.final_layer.linear.weight",
+                "flow_net.final_layer.linear.bias", lat, dim, true);
     }
     check_cuda(cudaStreamSynchronize(m->stream), "load");
   } catch (...) {
@@ -311,7 +356,7 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     s->am_val.alloc(cand * 4);
     s->am_idx.alloc(cand * 4);
     if (c.weight_dtype == SVL_DT_BF16 && max_batch >= kGemmMinBatch) {
-      const int kx = std::max(d, qd);
+      const int kx = std::max({d, qd, m->kind == 1 ? m->tts.flow_dim : 0, m->kind == 1 ? m->tts.latent_dim : 0});
       s->xa.alloc((int64_t)max_batch * kx * 2);
       s->xh.alloc((int64_t)max_batch * c.ffn_hidden * 2);
       check_cuda(cudaMemsetAsync(s->xa.p, 0, s->xa.bytes, m->stream), "memset");
@@ -345,6 +390,26 @@ State* create_state(Model* m, int max_batch, int max_positions) {
       s->h_tok_in.alloc(max_batch * 4);
       s->h_tok_out.alloc(max_batch * 4);
       s->h_audio_in.alloc((int64_t)max_batch * std::max(st.n_q, 1) * 4);
+    }
+    if (m->kind == 1) {
+      const auto& t = m->tts;
+      const int64_t B = max_batch, lat = t.latent_dim, dim = t.flow_dim;
+      s->latent_in.alloc(B * lat * 4);
+      s->noise.alloc(B * lat * 4);
+      s->latent_out.alloc(B * lat * 4);
+      s->tmp.alloc(B * lat * 4);
+      s->eos.alloc(B * 4);
+      s->z.alloc(B * d * 4);
+      s->y.alloc(B * dim * 4);
+      s->sy.alloc(B * dim * 4);
+      s->hbuf.alloc(B * dim * 4);
+      s->h2buf.alloc(B * dim * 4);
+      s->xs2.alloc(B * dim * 4);
+      s->modbuf.alloc(B * 3 * dim * 4);
+      s->temb_in.alloc(256 * 4);
+      s->temb_h.alloc(dim * 4);
+      s->temb_o.alloc(dim * 4);
+      s->tsum.alloc(dim * 4);
     }
     // tok_out holds each stream's last argmax (the text token a resumed stream feeds back).
     if (m->kind == 0) check_cuda(cudaMemsetAsync(s->tok_out.p, 0, max_batch * 4, m->stream), "memset");
@@ -625,6 +690,146 @@ int capture_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
 void launch_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
   capture_stt_graph(m, s, nb, st);
   check_cuda(cudaGraphLaunch(s.graphs[nb], st), "graph launch");
+}
+
+// ---- Pocket-TTS step ------------------------------------------------------------------
+
+namespace {
+
+// bf16 operand map over the state's xa buffer for rows of k elements, tiles of bn streams.
+const GemmOperand& xa_map(State& s, int k, int nb) {
+  const int bn = gemm_stream_tile(nb);
+  const int64_t key = (int64_t)k * 512 + bn;
+  auto it = s.xa_by_k.find(key);
+  if (it == s.xa_by_k.end()) {
+    GemmOperand op;
+    if (!make_gemm_operand(op, s.xa.p, s.max_batch, k, (int64_t)k * 2, bn))
+      throw Error(SVL_ERR_CUDA, "cannot encode a TMA tensor map of a GEMM operand");
+    it = s.xa_by_k.emplace(key, op).first;
+  }
+  return it->second;
+}
+
+// One weight product over streams [0, nb): out[b] = epi(L . x[b] + bias). The matrix-vector
+// kernel reads the f32 rows directly; for many bf16 streams the rows become bf16 operand rows
+// and the product runs on the tensor cores.
+void linear_fwd(Model& m, State& s, const Linear& L, const float* x, int64_t x_stride, int nb,
+                int epi, float* out, int64_t out_stride, cudaStream_t st) {
+  GemvParams g = gemv_base(L, x, x_stride, nb);
+  g.epi = epi;
+  g.out = out;
+  g.out_stride = out_stride;
+  if (use_tensor_cores(m, s, nb) && L.tc.valid) {
+    launch_prep_bf16(x, x_stride, nb, NORM_NONE, nullptr, nullptr, 0.f, L.k, s.xa.p, L.k, st);
+    launch_gemm(g, L.tc, xa_map(s, L.k, nb), 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
+  } else {
+    launch_gemv(g, st);
+  }
+}
+
+// FlowHead::forward (tts/flow_lm.rs:259-287) and decode (:290-315) from s.z into the latent
+// s.latent_out (which enters holding the noise).
+void enqueue_flow(Model& m, State& s, int nb, int steps, cudaStream_t st) {
+  const auto& t = m.tts;
+  const int dim = t.flow_dim, lat = t.latent_dim, d = m.cfg.d_model;
+  const int n_time = (int)m.time_emb.size();
+  float* y = s.y.as<float>();
+  float* sy = s.sy.as<float>();
+  float* xs = s.xs2.as<float>();
+  float* hh = s.hbuf.as<float>();
+  float* h2 = s.h2buf.as<float>();
+  float* mod = s.modbuf.as<float>();
+  float* x = s.latent_out.as<float>();
+  float* flow = s.tmp.as<float>();
+  // cond_embed does not depend on the decode step.
+  linear_fwd(m, s, m.cond_embed, s.z.as<float>(), d, nb, EPI_STORE, y, dim, st);
+  const int iters = n_time > 0 ? steps : 1;
+  for (int i = 0; i < iters; i++) {
+    if (n_time > 0) {
+      // TimestepEmbedder per time (lsd: i/steps and (i+1)/steps; flow matching: i/steps).
+      for (int e = 0; e < n_time; e++) {
+        const TimeEmbed& te = m.time_emb[e];
+        const float tv = (float)(i + e) / (float)steps;
+        launch_time_input(te.freqs.as<float>(), tv, s.temb_in.as<float>(), st);
+        GemvParams g = gemv_base(te.l1, s.temb_in.as<float>(), 256, 1);
+        g.epi = EPI_SILU;
+        g.out = s.temb_h.as<float>();
+        g.out_stride = dim;
+        launch_gemv(g, st);
+        g = gemv_base(te.l2, s.temb_h.as<float>(), dim, 1);
+        g.epi = EPI_STORE;
+        g.out = s.temb_o.as<float>();
+        g.out_stride = dim;
+        launch_gemv(g, st);
+        launch_time_norm(s.temb_o.as<float>(), dim, te.alpha.as<float>(), s.tsum.as<float>(), e == 0, st);
+      }
+    }
+    launch_cond_silu(y, n_time > 0 ? s.tsum.as<float>() : nullptr,
+                     n_time > 0 ? (float)(1.0 / (double)n_time) : 0.f, dim, nb, sy, st);
+    linear_fwd(m, s, m.input_proj, x, lat, nb, EPI_STORE, xs, dim, st);
+    for (const ResBlock& r : m.res) {
+      linear_fwd(m, s, r.mod, sy, dim, nb, EPI_STORE, mod, 3 * dim, st);
+      launch_adaln(xs, nb, dim, r.ln.w.as<float>(), r.ln.b.as<float>(), 1, r.ln.eps, mod, 3 * dim, hh, st);
+      linear_fwd(m, s, r.mlp1, hh, dim, nb, EPI_SILU, h2, dim, st);
+      linear_fwd(m, s, r.mlp2, h2, dim, nb, EPI_STORE, hh, dim, st);
+      launch_gate_add(xs, mod, 3 * dim, 2 * dim, hh, nb, dim, st);
+    }
+    linear_fwd(m, s, m.final_mod, sy, dim, nb, EPI_STORE, mod, 2 * dim, st);
+    launch_adaln(xs, nb, dim, nullptr, nullptr, 0, 1e-6f, mod, 2 * dim, hh, st);
+    linear_fwd(m, s, m.final_linear, hh, dim, nb, EPI_STORE, flow, lat, st);
+    const int mode = n_time > 0 ? 0 : t.flow_kind == 2 ? 1 : 2;
+    launch_flow_update(x, flow, (int64_t)nb * lat, mode, (float)(1.0 / (double)steps), st);
+  }
+}
+
+// FlowLm::step (tts/flow_lm.rs:162-185) for streams [0, nb).
+void enqueue_tts_step(Model& m, State& s, int nb, int steps, cudaStream_t st) {
+  const int d = m.cfg.d_model, lat = m.tts.latent_dim;
+  linear_fwd(m, s, m.input_linear, s.latent_in.as<float>(), lat, nb, EPI_STORE, s.x.as<float>(), d, st);
+  enqueue_layers(m, s, 0, nb, st);
+  launch_advance_positions(s.pos.as<int>(), nb, st);
+  launch_tts_head(s.x.as<float>(), nb, d, m.out_norm.w.as<float>(), m.out_norm.b.as<float>(),
+                  m.out_norm.eps, m.eos_w.as<float>(), m.eos_b.as<float>(), s.z.as<float>(),
+                  s.eos.as<float>(), st);
+  check_cuda(cudaMemcpyAsync(s.latent_out.p, s.noise.p, (size_t)nb * lat * 4,
+                             cudaMemcpyDeviceToDevice, st), "noise");
+  enqueue_flow(m, s, nb, steps, st);
+}
+
+}  // namespace
+
+void launch_tts_graph(Model& m, State& s, int nb, int steps, cudaStream_t st) {
+  const int key = nb + (steps << 16);
+  auto it = s.graphs.find(key);
+  if (it == s.graphs.end()) {
+    cudaGraph_t graph = nullptr;
+    check_cuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      enqueue_tts_step(m, s, nb, steps, st);
+    } catch (...) {
+      cudaStreamEndCapture(st, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    check_cuda(cudaStreamEndCapture(st, &graph), "end capture");
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    check_cuda(e, "graph instantiate");
+    it = s.graphs.emplace(key, exec).first;
+  }
+  check_cuda(cudaGraphLaunch(it->second, st), "graph launch");
+}
+
+void enqueue_tts_prompt(Model& m, State& s, int b0, int nb, const uint32_t* d_tokens, int n,
+                        cudaStream_t st) {
+  const int d = m.cfg.d_model;
+  for (int t = 0; t < n; t++) {
+    launch_prompt_embed(m.cond_table.as<float>(), d_tokens, nb, n, t, d, m.tts.text_bins,
+                        s.x.as<float>() + (int64_t)b0 * d, s.err.as<int>(), st);
+    enqueue_layers(m, s, b0, nb, st);
+    launch_advance_positions(s.pos.as<int>() + b0, nb, st);
+  }
 }
 
 int64_t enqueue_profile(Model& m, State& s, int nb, int which, cudaStream_t st) {

@@ -100,9 +100,10 @@ struct Model {
   Linear text_linear;
   std::vector<Linear> extra;
   // TTS
-  DevBuf cond_table;
-  Linear input_linear, out_eos;
-  DevBuf bos;
+  DevBuf cond_table;             // conditioner rows [text_bins + 1][d]
+  Linear input_linear;
+  DevBuf eos_w, eos_b;           // out_eos [d] and its bias [1]
+  DevBuf bos;                    // bos_emb [latent]
   std::vector<TimeEmbed> time_emb;
   Linear cond_embed, input_proj, final_mod, final_linear;
   std::vector<ResBlock> res;
@@ -127,6 +128,8 @@ struct State {
   DevBuf frames_audio, frames_out;  // svl_stt_run_frames
   // TTS work buffers
   DevBuf latent_in, noise, latent_out, eos, z, y, sy, hbuf, h2buf, modbuf, xs2, tmp;
+  DevBuf temb_in, temb_h, temb_o, tsum, prompt_tok;
+  std::map<int64_t, GemmOperand> xa_by_k;  // bf16 operand maps over xa, keyed by k * 512 + bn
   HostBuf h_tok_in, h_audio_in, h_tok_out;
   int splits = 1;
   // Tensor-core path (bf16 weights, many streams): bf16 operand rows and their TMA maps, per
@@ -157,6 +160,13 @@ void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st);
 void launch_stt_graph(Model& m, State& s, int nb, cudaStream_t st);
 // Captures the step graph of batch size nb if it is not captured yet; returns its kernels.
 int capture_stt_graph(Model& m, State& s, int nb, cudaStream_t st);
+// FlowLm::step (tts/flow_lm.rs:162-185) for streams [0, nb) from the state's latent_in /
+// noise buffers into latent_out / eos, as one graph per (nb, decode_steps).
+void launch_tts_graph(Model& m, State& s, int nb, int decode_steps, cudaStream_t st);
+// FlowLm::prompt_text (tts/flow_lm.rs:150-158) for streams [b0, b0 + nb): n tokens each,
+// device tokens [nb][n].
+void enqueue_tts_prompt(Model& m, State& s, int b0, int nb, const uint32_t* d_tokens, int n,
+                        cudaStream_t st);
 // Profiling: one repetition of the step's weight products (which 0) or attention (which 1).
 int64_t enqueue_profile(Model& m, State& s, int nb, int which, cudaStream_t st);
 void enqueue_tts_step(Model& m, State& s, int nb, int decode_steps, bool bos, cudaStream_t st);

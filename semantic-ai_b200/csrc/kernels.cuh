@@ -144,4 +144,21 @@ void launch_round_bf16_inplace(float* p, int64_t n, cudaStream_t s);
 
 int64_t packed_row_stride(int wtype, int k);
 
+// Pocket-TTS step pieces (tts.cu).
+void launch_tts_head(const float* x, int nb, int d, const float* lnw, const float* lnb, float eps,
+                     const float* w_eos, const float* b_eos, float* z, float* eos, cudaStream_t s);
+void launch_time_input(const float* freqs, float t, float* emb, cudaStream_t s);
+void launch_time_norm(const float* te, int dim, const float* alpha, float* tsum, int first,
+                      cudaStream_t s);
+void launch_cond_silu(const float* y, const float* tsum, float inv_n, int dim, int nb, float* sy,
+                      cudaStream_t s);
+void launch_adaln(const float* xs, int nb, int dim, const float* lnw, const float* lnb, int affine,
+                  float eps, const float* mod, int64_t mod_stride, float* hh, cudaStream_t s);
+void launch_gate_add(float* xs, const float* mod, int64_t mod_stride, int gate_off, const float* h,
+                     int nb, int dim, cudaStream_t s);
+void launch_flow_update(float* x, const float* flow, int64_t n, int mode, float scale,
+                        cudaStream_t s);
+void launch_prompt_embed(const float* table, const uint32_t* tokens, int nb, int n, int t, int d,
+                         int bins, float* x, int* err, cudaStream_t s);
+
 }  // namespace svl

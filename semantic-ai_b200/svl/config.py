@@ -152,6 +152,16 @@ def pocket_tts() -> tuple[TransformerConfig, TtsConfig]:
     return t, TtsConfig(latent_dim=32, flow_dim=512, flow_depth=6, flow_kind="lsd", text_bins=4000)
 
 
+def tts_toy(flow_kind: str = "lsd", weight_dtype: str = "f32", kv_dtype: str = "f32"):
+    """A small Pocket-TTS-shaped model for fast parity runs: d 128, 2 layers, 2 heads x 64,
+    GELU-tanh FFN 512, LayerNorm, no window; flow head width 64, depth 2, latent 32."""
+    t = TransformerConfig(d_model=128, num_layers=2, num_heads=2, num_kv_heads=2, head_dim=64,
+                          ffn_kind=FFN_PLAIN_GELU_TANH, ffn_hidden=512, norm_kind=NORM_LAYER,
+                          norm_eps=1e-5, layer_scale=False, context=None, max_period=10_000.0,
+                          weight_dtype=weight_dtype, kv_dtype=kv_dtype)
+    return t, TtsConfig(latent_dim=32, flow_dim=64, flow_depth=2, flow_kind=flow_kind, text_bins=50)
+
+
 def kv_bytes_per_stream(cfg: TransformerConfig, fill: int) -> int:
     el = 2 if cfg.kv_dtype == "bf16" else 4
     return cfg.num_layers * 2 * fill * cfg.num_kv_heads * cfg.head_dim * el

@@ -181,8 +181,15 @@ class FlowLm(_Model):
         del keep
 
     def prompt_text(self, tokens, state: State, stream: int = 0):
+        """FlowLm::prompt_text for one stream: tokens [n]."""
         t = np.ascontiguousarray(tokens, np.uint32)
         _lib.check(_lib.lib().svl_tts_prompt_text(self.handle, state.handle, stream, _u32(t), t.size))
+
+    def prompt_text_batch(self, tokens, state: State):
+        """FlowLm::prompt_text for streams 0..B-1 at once: tokens [B, n]."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        _lib.check(_lib.lib().svl_tts_prompt_text_batch(self.handle, state.handle, t.shape[0],
+                                                        _u32(t), t.shape[1]))
 
     def step(self, latent, noise, state: State, decode_steps: int = 1):
         """FlowLm::step for streams 0..B-1: latent [B, latent] (None = BOS), noise [B, latent]
