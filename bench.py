@@ -42,6 +42,8 @@ CONFIGS = {
               wdt="q4_1", kv="bf16", batch=1, frames=1500),
     "4b": dict(workload="stt-2.6b q4_1 128 streams/GPU (BASELINE config 4)", preset="stt_2b6",
                wdt="q4_1", kv="bf16", batch=128, frames=1500, stagger=375),
+    "5": dict(workload="pocket-tts bf16 512 streams/GPU, 64-token prompts (BASELINE config 5)",
+              kind="tts", wdt="bf16", kv="bf16", batch=512, frames=500, prompt=64),
 }
 
 
@@ -291,6 +293,187 @@ def run_ours(args, spec, rank, world, local_rank):
         print(json.dumps(out), flush=True)
 
 
+def tts_config(spec):
+    import dataclasses
+    cfg, tts = C.pocket_tts()
+    return dataclasses.replace(cfg, weight_dtype=spec["wdt"], kv_dtype=spec["kv"]), tts
+
+
+def run_tts(args, spec, rank, world, local_rank):
+    """FlowLm::step for every stream of the GPU per frame: a 64-token text prompt prefilled
+    per stream (FlowLm::prompt_text), then frames of latent feedback (LatentGenerator::advance,
+    tts/mod.rs:494) with the noise passed in as an input tensor (seed 4, temperature 1)."""
+    import torch
+    from svl import FlowLm
+    from svl import _lib
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    cfg, tts = tts_config(spec)
+    B, K, W, P = spec["batch"], args.steps, args.warmup, spec["prompt"]
+    weights = synth.tts_weights(cfg, tts, seed=0)
+    model = FlowLm(cfg, tts, weights, device=local_rank)
+    L = _lib.lib()
+    g0 = rank * B
+    tokens = np.stack([np.random.default_rng(3 + g0 + b).integers(0, tts.text_bins, size=P, dtype=np.uint32)
+                       for b in range(B)])
+    noise = np.random.default_rng(4 + rank).standard_normal((K + W, B, tts.latent_dim)).astype(np.float32)
+    dev = f"cuda:{local_rank}"
+    d_noise = torch.from_numpy(noise).to(dev)
+    lat = [torch.zeros((B, tts.latent_dim), dtype=torch.float32, device=dev) for _ in range(2)]
+    eos = torch.zeros(B, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream()
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    row = B * tts.latent_dim * 4
+
+    def fresh_state():
+        st = model.init_state(B, max_positions=P + K + W + 1)
+        model.prompt_text_batch(tokens, st)
+        return st
+
+    def device_steps(st, first, n):
+        for i in range(n):
+            src = None if first + i == 0 else ctypes.c_void_p(lat[i % 2].data_ptr())
+            _lib.check(L.svl_tts_step_device(model.handle, st.handle, B, src,
+                                             ctypes.c_void_p(d_noise.data_ptr() + (first + i) * row), 1,
+                                             ctypes.c_void_p(lat[(i + 1) % 2].data_ptr()),
+                                             ctypes.c_void_p(eos.data_ptr()), sptr))
+
+    st = fresh_state()
+    with torch.cuda.stream(stream):
+        device_steps(st, 0, W)
+    stream.synchronize()
+    st.close()
+    st = fresh_state()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        device_steps(st, 0, K)
+        e1.record(stream)
+    stream.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * B * K / (ms_max / 1000.0)
+    st.close()
+
+    # End to end through the host-buffer call: noise H2D, latent + EOS D2H every step.
+    st = fresh_state()
+    prev = None
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(K):
+        prev, _ = model.step(prev, noise[i], st)
+    e2e_s = time.perf_counter() - t0
+    t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * B * K / float(t.item())
+    st.close()
+
+    # Kernel families: transformer products, attention (at the run's mean fill), flow head.
+    peaks, peak_kind = load_peaks()
+    kern = {}
+    st = model.init_state(B, max_positions=P + K + W + 1)
+    fill = P + K // 2
+    for b in range(B):
+        _lib.check(L.svl_state_import(st.handle, b, 0, None, None, 0, fill))
+    names = {0: "products (transformer linears)", 1: "attention (all layers)", 2: "flow head"}
+    for which, name in names.items():
+        nbytes = ctypes.c_int64()
+        iters = 20
+        with torch.cuda.stream(stream):
+            _lib.check(L.svl_profile_kernels(model.handle, st.handle, B, which, 3, sptr, ctypes.byref(nbytes)))
+            stream.synchronize()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            _lib.check(L.svl_profile_kernels(model.handle, st.handle, B, which, iters, sptr, ctypes.byref(nbytes)))
+            a1.record(stream)
+        stream.synchronize()
+        per = a0.elapsed_time(a1) / iters
+        kern[name] = {"ms_per_step": per, "bytes_per_step": nbytes.value,
+                      "gbs": nbytes.value / (per / 1e3) / 1e9}
+    nk = ctypes.c_int32()
+    _lib.check(L.svl_step_kernel_count(model.handle, st.handle, B, ctypes.byref(nk)))
+    st.close()
+    dom = max(kern, key=lambda k: kern[k]["ms_per_step"])
+    hbm = peaks["hbm_gbs"]
+    n_launch_dom = cfg.num_layers if dom.startswith("attention") else None
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(kern[dom]["gbs"], 1), "peak": hbm,
+                "unit": "GB/s", "frac": round(kern[dom]["gbs"] / hbm, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "traffic": None, "launches_per_step": n_launch_dom,
+                "algorithmic_bytes_per_launch": kern[dom]["bytes_per_step"] // (n_launch_dom or 1)}
+    kv = B * C.kv_bytes_per_stream(cfg, P + K // 2)
+    step_bytes = model.weight_bytes + kv
+    step_frac = step_bytes / (ms_max / K / 1e3) / (hbm * 1e9)
+    out = {
+        "metric": "stream-frames/s", "value": round(value, 2), "unit": "stream-frames/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_max / K, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": spec["wdt"],
+        "data": "synthetic (random-init N(0,0.02) weights seed 0, prompt ids seed 3+stream, noise N(0,1) seed 4)",
+        "config": {"workload": spec["workload"], "streams_per_gpu": B, "frames": K, "prompt": P,
+                   "d_model": cfg.d_model, "layers": cfg.num_layers, "flow_depth": tts.flow_depth,
+                   "kv_dtype": cfg.kv_dtype,
+                   "parallelism": f"{world} GPU(s) x {B} independent streams, no collective",
+                   "l2": f"inputs larger than L2: {kv / 1e9:.2f} GB of KV read per step"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "stream-frames/s",
+                "h2d_bytes_per_step": B * tts.latent_dim * 4 * 2,
+                "d2h_bytes_per_step": B * (tts.latent_dim + 1) * 4},
+        "gpu_launches": nk.value * K,
+        "roofline": roofline,
+        "step_roofline": {"bytes_per_step": int(step_bytes), "frac": round(step_frac, 4),
+                          "unit": "of measured HBM GB/s"},
+        "kernels": kern,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline_tts(cfg, tts, weights, tokens[0], budget_s=args.cpu_seconds)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def cpu_baseline_tts(cfg, tts, weights, prompt, budget_s=15.0, frames_cap=None):
+    """The oracle's FlowLm step on the host's cores: stream 0's prompt, then frames until the
+    time budget is spent."""
+    import oracle as O
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    om = O.OracleModel(1, cfg, weights, tts=tts)
+    st = om.init_state()
+    om.prompt_text(prompt, st)
+    noise = np.random.default_rng(4).standard_normal((4096, tts.latent_dim)).astype(np.float32)
+    prev, n = None, 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and (frames_cap is None or n < frames_cap) and n < 4096:
+        prev, _ = om.tts_step(prev, noise[n], st)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "stream-frames/s", "cores": threads, "kind": "port",
+            "sample": f"{n} frames of one stream after a {len(prompt)}-token prompt ({cfg.weight_dtype} "
+                      f"weights), {dt:.1f} s on {threads} threads"}
+
+
 def cpu_baseline(spec, stt, cfg, weights, budget_s=15.0, frames_cap=None):
     """The oracle (a C restatement of the reference CPU path) on the host's cores: stream 0 of
     the workload from position 0, frames until the time budget is spent."""
@@ -317,6 +500,26 @@ def run_reference(args, spec, rank):
     """The reference's CPU implementation of the path: the oracle port (the Rust reference
     cannot be built in this image), all host threads, bounded samples of the workload."""
     if rank != 0:
+        return
+    if spec.get("kind") == "tts":
+        cfg, tts = tts_config(spec)
+        weights = synth.tts_weights(cfg, tts, seed=0)
+        prompt = np.random.default_rng(3).integers(0, tts.text_bins, size=spec["prompt"], dtype=np.uint32)
+        t0 = time.perf_counter()
+        cb = cpu_baseline_tts(cfg, tts, weights, prompt, budget_s=args.ref_seconds,
+                              frames_cap=args.steps + args.warmup)
+        value = cb["value"]
+        out = {"metric": "stream-frames/s", "value": value, "unit": "stream-frames/s",
+               "n_gpus": args.gpus, "steps": args.steps, "warmup": 0,
+               "ms_per_step": round(1e3 / max(value, 1e-9), 3), "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": spec["wdt"], "data": "synthetic",
+               "config": {"workload": spec["workload"], "streams_per_gpu": spec["batch"]},
+               "impl": "reference",
+               "cpu_baseline": dict(cb, sample=cb["sample"] + " (C restatement of the reference "
+                                    "CPU path; the Rust reference needs cargo and candle 0.11.1)"),
+               "e2e": {"value": value, "unit": "stream-frames/s", "h2d_bytes_per_step": 0,
+                       "d2h_bytes_per_step": 0}}
+        print(json.dumps(out), flush=True)
         return
     stt = preset(spec["preset"])
     cfg = stt.transformer(spec["wdt"], spec["kv"])
@@ -383,6 +586,8 @@ def main():
                  "--nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N")
     if args.impl == "reference":
         run_reference(args, spec, rank)
+    elif spec.get("kind") == "tts":
+        run_tts(args, spec, rank, world, local_rank)
     else:
         run_ours(args, spec, rank, world, local_rank)
 

@@ -181,10 +181,19 @@ SVL_API svl_status svl_tts_step(svl_model* model, svl_state* state, int32_t batc
                                 const float* latent_in, const float* noise, int32_t decode_steps,
                                 float* latent_out, float* eos_logit);
 
+/* The same step on device buffers, enqueued on `cuda_stream` (NULL = the model's stream)
+ * without host synchronisation; d_latent_in NULL = BOS. d_latent_in may be the previous
+ * call's d_latent_out (the latent feedback of LatentGenerator::advance, tts/mod.rs:494). */
+SVL_API svl_status svl_tts_step_device(svl_model* model, svl_state* state, int32_t batch,
+                                       const float* d_latent_in, const float* d_noise,
+                                       int32_t decode_steps, float* d_latent_out, float* d_eos,
+                                       void* cuda_stream);
+
 /* Profiling hook (no counterpart in the reference): enqueues `iters` repetitions of one
- * kernel family of the STT step for streams 0..batch-1 on `cuda_stream` so a caller can time
- * it with CUDA events on that stream. which = 0: every weight product of a step (the layer
- * linears and the head); which = 1: every layer's attention. The repetitions overwrite the
+ * kernel family of the step for streams 0..batch-1 on `cuda_stream` so a caller can time
+ * it with CUDA events on that stream. which = 0: every weight product of the transformer
+ * (the layer linears, and the head of an STT model); which = 1: every layer's attention;
+ * which = 2 (TTS models): the flow head with one decode step. The repetitions overwrite the
  * state's activations and KV slots at the current positions, so the state must be reset
  * before it is used again. *bytes_per_iter receives the algorithmic HBM bytes of one
  * repetition (weights, or the KV rows read at the current positions). */
@@ -192,9 +201,10 @@ SVL_API svl_status svl_profile_kernels(svl_model* model, svl_state* state, int32
                                        int32_t which, int32_t iters, void* cuda_stream,
                                        int64_t* bytes_per_iter);
 
-/* Kernels one svl_stt_step / svl_stt_step_device call launches at this batch size: the
- * kernel nodes of the step's CUDA graph, which this call captures if no step of that batch
- * size ran yet. Diagnostics only; no counterpart in the reference. */
+/* Kernels one step call (svl_stt_step[_device], or svl_tts_step[_device] with one decode
+ * step) launches at this batch size: the kernel nodes of the step's CUDA graph, which this
+ * call captures if no step of that batch size ran yet. Diagnostics only; no counterpart in
+ * the reference. */
 SVL_API svl_status svl_step_kernel_count(svl_model* model, svl_state* state, int32_t batch,
                                          int32_t* kernels);
 

@@ -337,10 +337,10 @@ SVL_API svl_status svl_profile_kernels(svl_model* model, svl_state* state, int32
     need(model && state, SVL_ERR_INVALID_INPUT, "null argument");
     svl::Model& m = *model->m;
     svl::State& s = *state->s;
-    need(m.kind == 0, SVL_ERR_INVALID_INPUT, "not an STT model");
     need(s.m == &m, SVL_ERR_INVALID_INPUT, "state of another model");
     need(batch >= 1 && batch <= s.max_batch, SVL_ERR_INVALID_INPUT, "batch out of range");
-    need(which == 0 || which == 1, SVL_ERR_INVALID_INPUT, "which must be 0 or 1");
+    need(which == 0 || which == 1 || (which == 2 && m.kind == 1), SVL_ERR_INVALID_INPUT,
+         "which must be 0 or 1 (2: the flow head of a TTS model)");
     need(iters >= 0, SVL_ERR_INVALID_INPUT, "negative iters");
     svl::check_cuda(cudaSetDevice(m.device), "cudaSetDevice");
     cudaStream_t st = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : m.stream;
@@ -361,11 +361,11 @@ SVL_API svl_status svl_step_kernel_count(svl_model* model, svl_state* state, int
     need(model && state && kernels, SVL_ERR_INVALID_INPUT, "null argument");
     svl::Model& m = *model->m;
     svl::State& s = *state->s;
-    need(m.kind == 0, SVL_ERR_INVALID_INPUT, "not an STT model");
     need(s.m == &m, SVL_ERR_INVALID_INPUT, "state of another model");
     need(batch >= 1 && batch <= s.max_batch, SVL_ERR_INVALID_INPUT, "batch out of range");
     svl::check_cuda(cudaSetDevice(m.device), "cudaSetDevice");
-    *kernels = svl::capture_stt_graph(m, s, batch, m.stream);
+    *kernels = m.kind == 0 ? svl::capture_stt_graph(m, s, batch, m.stream)
+                           : svl::capture_tts_graph(m, s, batch, 1, m.stream);
   });
 }
 
@@ -418,6 +418,38 @@ SVL_API svl_status svl_tts_prompt_text_batch(svl_model* model, svl_state* state,
   });
 }
 
+SVL_API svl_status svl_tts_step_device(svl_model* model, svl_state* state, int32_t batch,
+                                       const float* d_latent_in, const float* d_noise,
+                                       int32_t decode_steps, float* d_latent_out, float* d_eos,
+                                       void* cuda_stream) {
+  return guarded([&] {
+    need(model && state && d_noise && d_latent_out && d_eos, SVL_ERR_INVALID_INPUT, "null argument");
+    svl::Model& m = *model->m;
+    svl::State& s = *state->s;
+    need(m.kind == 1, SVL_ERR_INVALID_INPUT, "not a TTS model");
+    need(s.m == &m, SVL_ERR_INVALID_INPUT, "state of another model");
+    need(batch >= 1 && batch <= s.max_batch, SVL_ERR_INVALID_INPUT, "batch out of range");
+    const int steps = decode_steps < 1 ? 1 : decode_steps;
+    need(steps <= 64, SVL_ERR_INVALID_INPUT, "decode_steps above 64");
+    check_room(s, batch, 1);
+    svl::check_cuda(cudaSetDevice(m.device), "cudaSetDevice");
+    cudaStream_t st = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : m.stream;
+    const size_t row = (size_t)m.tts.latent_dim * 4;
+    if (d_latent_in) {
+      svl::check_cuda(cudaMemcpyAsync(s.latent_in.p, d_latent_in, row * batch, cudaMemcpyDeviceToDevice, st), "copy");
+    } else {
+      for (int b = 0; b < batch; b++)
+        svl::check_cuda(cudaMemcpyAsync(s.latent_in.as<uint8_t>() + row * b, m.bos.p, row,
+                                        cudaMemcpyDeviceToDevice, st), "bos");
+    }
+    svl::check_cuda(cudaMemcpyAsync(s.noise.p, d_noise, row * batch, cudaMemcpyDeviceToDevice, st), "copy");
+    svl::launch_tts_graph(m, s, batch, steps, st);
+    svl::check_cuda(cudaMemcpyAsync(d_latent_out, s.latent_out.p, row * batch, cudaMemcpyDeviceToDevice, st), "copy");
+    svl::check_cuda(cudaMemcpyAsync(d_eos, s.eos.p, (size_t)batch * 4, cudaMemcpyDeviceToDevice, st), "copy");
+    for (int b = 0; b < batch; b++) s.hpos[b]++;
+  });
+}
+
 SVL_API svl_status svl_tts_step(svl_model* model, svl_state* state, int32_t batch,
                                 const float* latent_in, const float* noise, int32_t decode_steps,
                                 float* latent_out, float* eos_logit) {
@@ -430,9 +462,7 @@ SVL_API svl_status svl_tts_step(svl_model* model, svl_state* state, int32_t batc
     need(batch >= 1 && batch <= s.max_batch, SVL_ERR_INVALID_INPUT, "batch out of range");
     const int steps = decode_steps < 1 ? 1 : decode_steps;  // FlowHead::decode runs >= 1 step
     need(steps <= 64, SVL_ERR_INVALID_INPUT, "decode_steps above 64");
-    for (int b = 0; b < batch; b++)
-      if (!s.windowed && s.hpos[b] + 1 > s.cap)
-        throw Error(SVL_ERR_INVALID_INPUT, "stream would exceed the state's max_positions");
+    check_room(s, batch, 1);
     svl::check_cuda(cudaSetDevice(m.device), "cudaSetDevice");
     cudaStream_t st = m.stream;
     const int lat = m.tts.latent_dim;

@@ -652,20 +652,24 @@ void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
   if (eh > 0) launch_extra_heads(s.extra_logits.as<float>(), nb, eh, edim, s.extra_p.as<float>(), st);
 }
 
-int capture_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
-  auto it = s.graphs.find(nb);
-  if (it != s.graphs.end()) return s.graph_kernels[nb];
+namespace {
+
+// Captures fn's launches on st into a graph stored under key (if not captured yet); returns
+// the graph's kernel nodes (the launches one replay makes).
+template <class F>
+int capture_graph(State& s, int key, cudaStream_t st, F&& fn) {
+  auto it = s.graphs.find(key);
+  if (it != s.graphs.end()) return s.graph_kernels[key];
   cudaGraph_t graph = nullptr;
   check_cuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture");
   try {
-    enqueue_stt_step(m, s, nb, st);
+    fn();
   } catch (...) {
     cudaStreamEndCapture(st, &graph);
     if (graph) cudaGraphDestroy(graph);
     throw;
   }
   check_cuda(cudaStreamEndCapture(st, &graph), "end capture");
-  // Count the kernel nodes: the launches one replay of the step makes.
   size_t n = 0;
   int kernels = 0;
   cudaError_t e = cudaGraphGetNodes(graph, nullptr, &n);
@@ -682,9 +686,15 @@ int capture_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
   if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
   cudaGraphDestroy(graph);
   check_cuda(e, "graph instantiate");
-  s.graphs.emplace(nb, exec);
-  s.graph_kernels[nb] = kernels;
+  s.graphs.emplace(key, exec);
+  s.graph_kernels[key] = kernels;
   return kernels;
+}
+
+}  // namespace
+
+int capture_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
+  return capture_graph(s, nb, st, [&] { enqueue_stt_step(m, s, nb, st); });
 }
 
 void launch_stt_graph(Model& m, State& s, int nb, cudaStream_t st) {
@@ -798,27 +808,13 @@ void enqueue_tts_step(Model& m, State& s, int nb, int steps, cudaStream_t st) {
 
 }  // namespace
 
+int capture_tts_graph(Model& m, State& s, int nb, int steps, cudaStream_t st) {
+  return capture_graph(s, nb + (steps << 16), st, [&] { enqueue_tts_step(m, s, nb, steps, st); });
+}
+
 void launch_tts_graph(Model& m, State& s, int nb, int steps, cudaStream_t st) {
-  const int key = nb + (steps << 16);
-  auto it = s.graphs.find(key);
-  if (it == s.graphs.end()) {
-    cudaGraph_t graph = nullptr;
-    check_cuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture");
-    try {
-      enqueue_tts_step(m, s, nb, steps, st);
-    } catch (...) {
-      cudaStreamEndCapture(st, &graph);
-      if (graph) cudaGraphDestroy(graph);
-      throw;
-    }
-    check_cuda(cudaStreamEndCapture(st, &graph), "end capture");
-    cudaGraphExec_t exec = nullptr;
-    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    check_cuda(e, "graph instantiate");
-    it = s.graphs.emplace(key, exec).first;
-  }
-  check_cuda(cudaGraphLaunch(it->second, st), "graph launch");
+  capture_tts_graph(m, s, nb, steps, st);
+  check_cuda(cudaGraphLaunch(s.graphs[nb + (steps << 16)], st), "graph launch");
 }
 
 void enqueue_tts_prompt(Model& m, State& s, int b0, int nb, const uint32_t* d_tokens, int n,
@@ -836,10 +832,20 @@ int64_t enqueue_profile(Model& m, State& s, int nb, int which, cudaStream_t st) 
   const auto& c = m.cfg;
   if (which == 0) {
     enqueue_layers_mask(m, s, 0, nb, st, true, false);
-    launch_head(m, s, head_params(m, s, nb), st);
-    int64_t bytes = m.text_linear.bytes();
+    int64_t bytes = 0;
     for (const Layer& L : m.layers)
       bytes += L.in_proj.bytes() + L.out_proj.bytes() + L.ff1.bytes() + L.ff2.bytes();
+    if (m.kind == 0) {
+      launch_head(m, s, head_params(m, s, nb), st);
+      bytes += m.text_linear.bytes();
+    }
+    return bytes;
+  }
+  if (which == 2) {
+    enqueue_flow(m, s, nb, 1, st);
+    int64_t bytes = m.cond_embed.bytes() + m.input_proj.bytes() + m.final_mod.bytes() + m.final_linear.bytes();
+    for (const ResBlock& r : m.res) bytes += r.mod.bytes() + r.mlp1.bytes() + r.mlp2.bytes();
+    for (const TimeEmbed& e : m.time_emb) bytes += e.l1.bytes() + e.l2.bytes();
     return bytes;
   }
   enqueue_layers_mask(m, s, 0, nb, st, false, true);

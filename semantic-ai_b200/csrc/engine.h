@@ -163,6 +163,7 @@ int capture_stt_graph(Model& m, State& s, int nb, cudaStream_t st);
 // FlowLm::step (tts/flow_lm.rs:162-185) for streams [0, nb) from the state's latent_in /
 // noise buffers into latent_out / eos, as one graph per (nb, decode_steps).
 void launch_tts_graph(Model& m, State& s, int nb, int decode_steps, cudaStream_t st);
+int capture_tts_graph(Model& m, State& s, int nb, int decode_steps, cudaStream_t st);
 // FlowLm::prompt_text (tts/flow_lm.rs:150-158) for streams [b0, b0 + nb): n tokens each,
 // device tokens [nb][n].
 void enqueue_tts_prompt(Model& m, State& s, int b0, int nb, const uint32_t* d_tokens, int n,

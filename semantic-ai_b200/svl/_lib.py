@@ -42,6 +42,7 @@ SIGNATURES = {
     "svl_tts_prompt_text": (_I, [_P, _P, _I, _U32P, _I]),
     "svl_tts_prompt_text_batch": (_I, [_P, _P, _I, _U32P, _I]),
     "svl_tts_step": (_I, [_P, _P, _I, _F32P, _F32P, _I, _F32P, _F32P]),
+    "svl_tts_step_device": (_I, [_P, _P, _I, _P, _P, _I, _P, _P, _P]),
     "svl_profile_kernels": (_I, [_P, _P, _I, _I, _I, _P, ctypes.POINTER(ctypes.c_int64)]),
     "svl_step_kernel_count": (_I, [_P, _P, _I, ctypes.POINTER(ctypes.c_int32)]),
     "svl_stt_head_noalloc": (_I, [_P, _I, _P, _P, _P, _P]),
