@@ -201,6 +201,12 @@ SVL_API svl_status svl_profile_kernels(svl_model* model, svl_state* state, int32
                                        int32_t which, int32_t iters, void* cuda_stream,
                                        int64_t* bytes_per_iter);
 
+/* The device-side error flag of a state, for callers of the *_device entry points (the
+ * host-buffer calls check it themselves): waits for the device, then returns
+ * SVL_ERR_INVALID_INPUT if a token id out of range reached the device, SVL_ERR_TIMEOUT if a
+ * bounded device-side wait ran out, SVL_OK otherwise; the flag is cleared. */
+SVL_API svl_status svl_state_error(svl_state* state);
+
 /* Kernels one step call (svl_stt_step[_device], or svl_tts_step[_device] with one decode
  * step) launches at this batch size: the kernel nodes of the step's CUDA graph, which this
  * call captures if no step of that batch size ran yet. Diagnostics only; no counterpart in

@@ -214,9 +214,11 @@ SVL_API svl_status svl_stt_step(svl_model* model, svl_state* state, int32_t batc
       svl::check_cuda(cudaMemcpyAsync(out_logits, s.logits.p, (size_t)batch * m.stt.text_card * 4, cudaMemcpyDeviceToHost, st), "d2h");
     if (out_extra && m.stt.extra_heads_num > 0)
       svl::check_cuda(cudaMemcpyAsync(out_extra, s.extra_p.p, (size_t)batch * m.stt.extra_heads_num * 4, cudaMemcpyDeviceToHost, st), "d2h");
+    svl::queue_error_read(s, st);
     svl::check_cuda(cudaStreamSynchronize(st), "step");
     std::memcpy(out_tokens, s.h_tok_out.p, batch * 4);
     for (int b = 0; b < batch; b++) s.hpos[b]++;
+    svl::raise_device_error(s, st);
   });
 }
 
@@ -297,8 +299,10 @@ SVL_API svl_status svl_stt_run_frames(svl_model* model, svl_state* state, int32_
                                       cudaMemcpyDeviceToDevice, st), "copy");
     }
     svl::check_cuda(cudaMemcpyAsync(out_tokens, s.frames_out.p, obytes, cudaMemcpyDeviceToHost, st), "d2h");
+    svl::queue_error_read(s, st);
     svl::check_cuda(cudaStreamSynchronize(st), "frames");
     for (int b = 0; b < batch; b++) s.hpos[b] += n_frames;
+    svl::raise_device_error(s, st);
   });
 }
 
@@ -352,6 +356,18 @@ SVL_API svl_status svl_profile_kernels(svl_model* model, svl_state* state, int32
     }
     if (bytes_per_iter) *bytes_per_iter = bytes;
     svl::check_cuda(cudaGetLastError(), "profile launch");
+  });
+}
+
+SVL_API svl_status svl_state_error(svl_state* state) {
+  return guarded([&] {
+    need(state, SVL_ERR_INVALID_INPUT, "null argument");
+    svl::State& s = *state->s;
+    svl::check_cuda(cudaSetDevice(s.m->device), "cudaSetDevice");
+    svl::check_cuda(cudaDeviceSynchronize(), "sync");
+    svl::queue_error_read(s, s.m->stream);
+    svl::check_cuda(cudaStreamSynchronize(s.m->stream), "sync");
+    svl::raise_device_error(s, s.m->stream);
   });
 }
 
@@ -479,8 +495,10 @@ SVL_API svl_status svl_tts_step(svl_model* model, svl_state* state, int32_t batc
     svl::launch_tts_graph(m, s, batch, steps, st);
     svl::check_cuda(cudaMemcpyAsync(latent_out, s.latent_out.p, row * batch, cudaMemcpyDeviceToHost, st), "d2h");
     svl::check_cuda(cudaMemcpyAsync(eos_logit, s.eos.p, (size_t)batch * 4, cudaMemcpyDeviceToHost, st), "d2h");
+    svl::queue_error_read(s, st);
     svl::check_cuda(cudaStreamSynchronize(st), "tts step");
     for (int b = 0; b < batch; b++) s.hpos[b] += 1;
+    svl::raise_device_error(s, st);
   });
 }
 

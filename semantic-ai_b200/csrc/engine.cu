@@ -1,7 +1,9 @@
 // engine.cu — weight loading, per-stream state and the step sequence of the LM.
 #include "engine.h"
+#include "gemv_common.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -227,6 +229,7 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
   check_cuda(cudaSetDevice(device), "cudaSetDevice");
   gemv_init_device();
   gemm_init_device();
+  step_kernel_init_device();
   attention_init_device();
   Model* m = new Model();
   try {
@@ -316,6 +319,32 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
   return m;
 }
 
+void build_step_program(Model& m, State& s);
+
+void queue_error_read(State& s, cudaStream_t st) {
+  check_cuda(cudaMemcpyAsync(s.h_err.p, s.err.p, 4, cudaMemcpyDeviceToHost, st), "d2h");
+}
+
+void raise_device_error(State& s, cudaStream_t st) {
+  const int e = *s.h_err.as<int>();
+  if (!e) return;
+  *s.h_err.as<int>() = 0;
+  check_cuda(cudaMemsetAsync(s.err.p, 0, 4, st), "memset");
+  check_cuda(cudaStreamSynchronize(st), "sync");
+  if (e == 1) throw Error(SVL_ERR_INVALID_INPUT, "a token id out of range reached the device");
+  throw Error(SVL_ERR_TIMEOUT, "a bounded device-side wait ran out (code " + std::to_string(e) + ")");
+}
+
+// SVL_STEP_KERNEL=1 runs the batch-1 step as the persistent step kernel (stepk.cu), read when
+// a state is created. It is off by default: on B200 it measures 0.76 ms per STT-1b q8_0 step
+// against 0.74 ms for the separate-kernel path. Its producer alone streams the step's bytes
+// in 215 us (78% of HBM); the consumers are latency-bound between the grid-wide phase
+// barriers (82 per step), which is the work left on it.
+bool step_kernel_disabled() {
+  const char* v = std::getenv("SVL_STEP_KERNEL");
+  return !(v && v[0] == '1');
+}
+
 State* create_state(Model* m, int max_batch, int max_positions) {
   if (max_batch <= 0) throw Error(SVL_ERR_INVALID_INPUT, "max_batch must be positive");
   check_cuda(cudaSetDevice(m->device), "cudaSetDevice");
@@ -376,6 +405,8 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     check_cuda(cudaMemsetAsync(s->am_ticket.p, 0, 4, m->stream), "memset");
     s->err.alloc(4);
     check_cuda(cudaMemsetAsync(s->err.p, 0, 4, m->stream), "memset");
+    s->h_err.alloc(4);
+    *s->h_err.as<int>() = 0;
 
     if (m->kind == 0) {
       const auto& st = m->stt;
@@ -413,6 +444,7 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     }
     // tok_out holds each stream's last argmax (the text token a resumed stream feeds back).
     if (m->kind == 0) check_cuda(cudaMemsetAsync(s->tok_out.p, 0, max_batch * 4, m->stream), "memset");
+    if (m->kind == 0 && !step_kernel_disabled()) build_step_program(*m, *s);
     check_cuda(cudaStreamSynchronize(m->stream), "state init");
   } catch (...) {
     delete s;
@@ -478,8 +510,9 @@ void enqueue_layers(Model& m, State& s, int b0, int nb, cudaStream_t st) {
   enqueue_layers_mask(m, s, b0, nb, st, true, true);
 }
 
-void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bool do_lin,
-                         bool do_attn) {
+// The parameter blocks of layer l's kernels for streams [b0, b0 + nb): in_proj + RoPE + KV
+// write, attention, out_proj + residual, linear_in + activation, linear_out + residual.
+LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   const auto& c = m.cfg;
   const int d = c.d_model, hd = c.head_dim, qd = c.num_heads * hd, kvd = c.num_kv_heads * hd;
   float* x = s.x.as<float>() + (int64_t)b0 * d;
@@ -487,33 +520,90 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
   float* attn = s.attn.as<float>() + (int64_t)b0 * qd;
   float* act = s.act.as<float>() + (int64_t)b0 * c.ffn_hidden;
   const int* pos = s.pos.as<int>() + b0;
+  const Layer& L = m.layers[l];
+  uint8_t* kr = s.k_ring.as<uint8_t>() + ((int64_t)l * s.ring_layer_stride + (int64_t)b0 * s.ring_stream_stride) * s.kv_elt;
+  uint8_t* vr = s.v_ring.as<uint8_t>() + ((int64_t)l * s.ring_layer_stride + (int64_t)b0 * s.ring_stream_stride) * s.kv_elt;
+  LayerParams lp;
+  // norm1 + in_proj + RoPE + KV-ring write (nn/transformer.rs:329-342).
+  GemvParams g = gemv_base(L.in_proj, x, d, nb);
+  set_norm(g, L.norm1);
+  g.epi = EPI_QKV_ROPE;
+  g.out = q;
+  g.out_stride = qd;
+  g.inv_freq = m.inv_freq.as<float>();
+  g.pos = pos;
+  g.q_dim = qd;
+  g.kv_dim = kvd;
+  g.head_dim = hd;
+  g.ring_cap = s.cap;
+  g.windowed = s.windowed;
+  g.k_ring = kr;
+  g.v_ring = vr;
+  g.ring_stream_stride = s.ring_stream_stride;
+  g.kv_bf16 = s.kv_elt == 2;
+  set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.in_proj; });
+  lp.in_proj = g;
+  // Sliding-window attention (nn/kernels/attention.rs:81-169).
+  AttnParams& a = lp.attn;
+  a = AttnParams{};
+  a.q = q;
+  a.k_ring = kr;
+  a.v_ring = vr;
+  a.ring_stream_stride = s.ring_stream_stride;
+  a.kv_bf16 = s.kv_elt == 2;
+  a.pos = pos;
+  a.nb = nb;
+  a.heads = c.num_heads;
+  a.kv_heads = c.num_kv_heads;
+  a.head_dim = hd;
+  a.ring_cap = s.cap;
+  a.window = c.context;
+  a.scale = std::pow((float)hd, -0.5f);
+  a.splits = s.splits;
+  a.out = attn;
+  a.err = s.err.as<int>();
+  // out_proj + residual (nn/transformer.rs:344, :239-243).
+  g = gemv_base(L.out_proj, attn, qd, nb);
+  g.epi = EPI_RESIDUAL;
+  g.out = x;
+  g.out_stride = d;
+  g.ls = L.ls1.as<float>();
+  set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.out_proj; });
+  lp.out_proj = g;
+  // norm2 + feed-forward (nn/transformer.rs:438-464).
+  g = gemv_base(L.ff1, x, d, nb);
+  set_norm(g, L.norm2);
+  g.out = act;
+  g.out_stride = c.ffn_hidden;
+  g.epi = c.ffn_kind == SVL_FFN_GATED_SILU ? EPI_SWIGLU
+          : c.ffn_kind == SVL_FFN_PLAIN_GELU_ERF ? EPI_GELU_ERF : EPI_GELU_TANH;
+  set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.ff1; });
+  lp.ff1 = g;
+  g = gemv_base(L.ff2, act, c.ffn_hidden, nb);
+  g.epi = EPI_RESIDUAL;
+  g.out = x;
+  g.out_stride = d;
+  g.ls = L.ls2.as<float>();
+  set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.ff2; });
+  lp.ff2 = g;
+  return lp;
+}
+
+void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bool do_lin,
+                         bool do_attn) {
+  const auto& c = m.cfg;
+  const int d = c.d_model, hd = c.head_dim, qd = c.num_heads * hd;
+  float* x = s.x.as<float>() + (int64_t)b0 * d;
+  const int* pos = s.pos.as<int>() + b0;
   const bool tc = use_tensor_cores(m, s, nb);
   const int ti = tc ? tile_index(nb) : 0;
   float2* rope_cs = tc ? s.rope_cs.as<float2>() + (int64_t)b0 * (hd / 2) : nullptr;
   if (tc && do_lin) launch_rope_table(pos, nb, m.inv_freq.as<float>(), hd / 2, rope_cs, st);
   for (int l = 0; l < c.num_layers; l++) {
     const Layer& L = m.layers[l];
-    uint8_t* kr = s.k_ring.as<uint8_t>() + ((int64_t)l * s.ring_layer_stride + (int64_t)b0 * s.ring_stream_stride) * s.kv_elt;
-    uint8_t* vr = s.v_ring.as<uint8_t>() + ((int64_t)l * s.ring_layer_stride + (int64_t)b0 * s.ring_stream_stride) * s.kv_elt;
-    // norm1 + in_proj + RoPE + KV-ring write (nn/transformer.rs:329-342).
-    GemvParams g = gemv_base(L.in_proj, x, d, nb);
-    set_norm(g, L.norm1);
-    g.epi = EPI_QKV_ROPE;
-    g.out = q;
-    g.out_stride = qd;
-    g.inv_freq = m.inv_freq.as<float>();
+    LayerParams lp = layer_params(m, s, l, b0, nb);
+    GemvParams g = lp.in_proj;
     g.rope_cs = rope_cs;
-    g.pos = pos;
-    g.q_dim = qd;
-    g.kv_dim = kvd;
-    g.head_dim = hd;
-    g.ring_cap = s.cap;
-    g.windowed = s.windowed;
-    g.k_ring = kr;
-    g.v_ring = vr;
-    g.ring_stream_stride = s.ring_stream_stride;
-    g.kv_bf16 = s.kv_elt == 2;
-    set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.in_proj; });
     if (do_lin && tc) {
       launch_prep_bf16(x, d, nb, L.norm1.kind, L.norm1.w.as<float>(), L.norm1.b.as<float>(),
                        L.norm1.eps, d, s.xa.p, d, st);
@@ -521,47 +611,16 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     } else if (do_lin) {
       launch_gemv(g, st);
     }
-    // Sliding-window attention (nn/kernels/attention.rs:81-169).
-    AttnParams a{};
-    a.q = q;
-    a.k_ring = kr;
-    a.v_ring = vr;
-    a.ring_stream_stride = s.ring_stream_stride;
-    a.kv_bf16 = s.kv_elt == 2;
-    a.pos = pos;
-    a.nb = nb;
-    a.heads = c.num_heads;
-    a.kv_heads = c.num_kv_heads;
-    a.head_dim = hd;
-    a.ring_cap = s.cap;
-    a.window = c.context;
-    a.scale = std::pow((float)hd, -0.5f);
-    a.splits = s.splits;
-    a.out = attn;
-    a.err = s.err.as<int>();
-    if (do_attn) launch_attention_decode(a, st);
+    if (do_attn) launch_attention_decode(lp.attn, st);
     if (!do_lin) continue;
-    // out_proj + residual (nn/transformer.rs:344, :239-243).
-    g = gemv_base(L.out_proj, attn, qd, nb);
-    g.epi = EPI_RESIDUAL;
-    g.out = x;
-    g.out_stride = d;
-    g.ls = L.ls1.as<float>();
-    set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.out_proj; });
+    g = lp.out_proj;
     if (tc) {
-      launch_prep_bf16(attn, qd, nb, NORM_NONE, nullptr, nullptr, 0.f, qd, s.xa.p, qd, st);
+      launch_prep_bf16(lp.attn.out, qd, nb, NORM_NONE, nullptr, nullptr, 0.f, qd, s.xa.p, qd, st);
       launch_gemm(g, L.out_proj.tc, s.xa_q[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
     } else {
       launch_gemv(g, st);
     }
-    // norm2 + feed-forward (nn/transformer.rs:438-464).
-    g = gemv_base(L.ff1, x, d, nb);
-    set_norm(g, L.norm2);
-    g.out = act;
-    g.out_stride = c.ffn_hidden;
-    g.epi = c.ffn_kind == SVL_FFN_GATED_SILU ? EPI_SWIGLU
-            : c.ffn_kind == SVL_FFN_PLAIN_GELU_ERF ? EPI_GELU_ERF : EPI_GELU_TANH;
-    set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.ff1; });
+    g = lp.ff1;
     if (tc) {
       launch_prep_bf16(x, d, nb, L.norm2.kind, L.norm2.w.as<float>(), L.norm2.b.as<float>(),
                        L.norm2.eps, d, s.xa.p, d, st);
@@ -570,12 +629,7 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     } else {
       launch_gemv(g, st);
     }
-    g = gemv_base(L.ff2, act, c.ffn_hidden, nb);
-    g.epi = EPI_RESIDUAL;
-    g.out = x;
-    g.out_stride = d;
-    g.ls = L.ls2.as<float>();
-    set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.ff2; });
+    g = lp.ff2;
     if (tc)
       launch_gemm(g, L.ff2.tc, s.xh_f[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
     else
@@ -603,6 +657,86 @@ GemvParams head_params(Model& m, State& s, int nb) {
 
 }  // namespace
 
+// Builds the persistent batch-1 step for stream 0 when the model fits its limits: an STT model
+// without extra heads, one weight format, k <= 10240, head_dim a multiple of 32 up to 128, and
+// at most 1024 keys per attention part. Otherwise step_ctas stays 0.
+void build_step_program(Model& m, State& s) {
+  const auto& c = m.cfg;
+  if (m.kind != 0 || m.stt.extra_heads_num > 0 || c.head_dim % 32 || c.head_dim > 128) return;
+  const int wt = m.text_linear.wtype;
+  const int ctas = step_kernel_ctas(wt);
+  if (ctas < c.num_heads) return;
+  std::vector<StepPhase> ph;
+  int64_t slot = 16 * 1024, rec = 0;
+  auto add_gemv = [&](const GemvParams& g) {
+    if (g.wtype != wt || g.k > 10240) return false;
+    const bool pairs = g.epi == EPI_QKV_ROPE || g.epi == EPI_SWIGLU;
+    slot = std::max<int64_t>(slot, (pairs ? 2 : 1) * g.row_stride);
+    rec = std::max<int64_t>(rec, rec_bytes_of(wt, g.k));
+    StepPhase p{};
+    p.type = PH_GEMV;
+    p.g = g;
+    p.g.pf = nullptr;
+    p.g.pf_bytes = 0;
+    ph.push_back(p);
+    return true;
+  };
+  StepPhase e{};
+  e.type = PH_EMBED;
+  e.e.text_table = m.text_emb.p;
+  e.e.audio_tables = m.audio_emb.p;
+  e.e.tables_bf16 = m.tables_bf16;
+  e.e.text_tok = s.tok_in.as<uint32_t>();
+  e.e.audio_tok = s.audio_in.as<uint32_t>();
+  e.e.nb = 1;
+  e.e.d = c.d_model;
+  e.e.n_q = m.stt.n_q;
+  e.e.card = m.stt.card;
+  e.e.text_card = m.stt.text_card;
+  e.e.x = s.x.as<float>();
+  e.e.error_flag = s.err.as<int>();
+  ph.push_back(e);
+  const int splits = std::max(1, ctas / c.num_heads);
+  const int keys = c.context > 0 ? c.context : s.cap;
+  if ((keys + splits - 1) / splits > 1024) return;
+  for (int l = 0; l < c.num_layers; l++) {
+    LayerParams lp = layer_params(m, s, l, 0, 1);
+    if (!add_gemv(lp.in_proj)) return;
+    StepPhase a{};
+    a.type = PH_ATTN;
+    a.a = lp.attn;
+    ph.push_back(a);
+    if (!add_gemv(lp.out_proj) || !add_gemv(lp.ff1) || !add_gemv(lp.ff2)) return;
+  }
+  GemvParams h = head_params(m, s, 1);
+  h.pos_advance = s.pos.as<int>();
+  if (!add_gemv(h)) return;
+  slot = (slot + 15) / 16 * 16;
+  rec = std::max<int64_t>((rec + 15) / 16 * 16, (int64_t)(1 + m.stt.n_q) * 16 * ((c.d_model / 4 + ctas - 1) / ctas));
+  const int nslots = (int)std::min<int64_t>(16, (kStepDynSmem - rec) / slot);
+  if (nslots < 4 || rec > kStepRecBytes) return;
+  s.step_phases.alloc(ph.size() * sizeof(StepPhase));
+  check_cuda(cudaMemcpyAsync(s.step_phases.p, ph.data(), ph.size() * sizeof(StepPhase),
+                             cudaMemcpyHostToDevice, m.stream), "upload");
+  s.step_counter_bytes = (ph.size() + (size_t)c.num_layers * c.num_heads) * 4;
+  s.step_counters.alloc(s.step_counter_bytes);
+  check_cuda(cudaMemsetAsync(s.step_counters.p, 0, s.step_counter_bytes, m.stream), "memset");
+  s.step_part.alloc((size_t)c.num_heads * splits * (c.head_dim + 2) * 4);
+  check_cuda(cudaStreamSynchronize(m.stream), "step program");
+  StepProgram& pg = s.step_pg;
+  pg.ph = s.step_phases.as<StepPhase>();
+  pg.nph = (int)ph.size();
+  pg.done = s.step_counters.as<unsigned>();
+  pg.head_cnt = pg.done + ph.size();
+  pg.part = s.step_part.as<float>();
+  pg.splits = splits;
+  pg.slot_bytes = (int)slot;
+  pg.nslots = nslots;
+  pg.rec_bytes = (int)rec;
+  pg.err = s.err.as<int>();
+  s.step_ctas = ctas;
+}
+
 // The logits product with its argmax: on the tensor cores (out_norm as the operand prep)
 // when the step's products run there.
 void launch_head(Model& m, State& s, const GemvParams& g, cudaStream_t st) {
@@ -618,6 +752,13 @@ void launch_head(Model& m, State& s, const GemvParams& g, cudaStream_t st) {
 
 void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
   const auto& c = m.cfg;
+  if (nb == 1 && s.step_ctas > 0) {
+    // The whole batch-1 step as one persistent kernel (stepk.cu).
+    check_cuda(cudaMemsetAsync(s.step_counters.p, 0, s.step_counter_bytes, st), "memset");
+    launch_step_kernel(s.step_pg, m.text_linear.wtype, s.step_ctas, st);
+    check_cuda(cudaGetLastError(), "step kernel launch");
+    return;
+  }
   const int d = c.d_model;
   EmbedParams e{};
   e.text_table = m.text_emb.p;

@@ -130,7 +130,7 @@ struct State {
   DevBuf latent_in, noise, latent_out, eos, z, y, sy, hbuf, h2buf, modbuf, xs2, tmp;
   DevBuf temb_in, temb_h, temb_o, tsum, prompt_tok;
   std::map<int64_t, GemmOperand> xa_by_k;  // bf16 operand maps over xa, keyed by k * 512 + bn
-  HostBuf h_tok_in, h_audio_in, h_tok_out;
+  HostBuf h_tok_in, h_audio_in, h_tok_out, h_err;
   int splits = 1;
   // Tensor-core path (bf16 weights, many streams): bf16 operand rows and their TMA maps, per
   // stream-tile width (64, 128, 256). xa holds normalised inputs / attention outputs, xh the
@@ -140,12 +140,29 @@ struct State {
   GemmOperand xa_d[3], xa_q[3], xh_f[3];
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, int> graph_kernels;  // kernel nodes of each captured step graph
+  // The persistent batch-1 step (stepk.cu): its phase program and counters, when it applies.
+  DevBuf step_phases, step_counters, step_part;
+  StepProgram step_pg{};
+  int step_ctas = 0;        // 0: the batch-1 step runs as separate kernels
+  size_t step_counter_bytes = 0;
   ~State();
+};
+
+// Parameter blocks of one layer's kernels (see layer_params).
+struct LayerParams {
+  GemvParams in_proj, out_proj, ff1, ff2;
+  AttnParams attn;
 };
 
 // Streams from which a step's weight products run on the tensor cores (bf16 weights).
 constexpr int kGemmMinBatch = 16;
 bool use_tensor_cores(const Model& m, const State& s, int nb);
+
+// The state's device error flag: queue its read (before the stream synchronises), then raise
+// it as an Error after the synchronisation (1: an id out of range on the device, 2 / 3: a
+// bounded device wait ran out). The flag is cleared when raised.
+void queue_error_read(State& s, cudaStream_t st);
+void raise_device_error(State& s, cudaStream_t st);
 
 // Weight loading (LanguageModel::new / FlowLm::new).
 Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_config* stt,

@@ -135,6 +135,33 @@ void launch_advance_positions(int* pos, int nb, cudaStream_t s);
 void launch_rope_table(const int* pos, int nb, const float* inv_freq, int half, float2* cs,
                        cudaStream_t s);
 
+// The persistent batch-1 step (stepk.cu): the step as a program of phases, each run by every
+// CTA on its share of rows / keys, with a grid-wide counter between phases.
+enum StepPhaseType { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
+struct StepPhase {
+  int type;
+  GemvParams g;   // PH_GEMV (nb = 1)
+  AttnParams a;   // PH_ATTN (nb = 1)
+  EmbedParams e;  // PH_EMBED (nb = 1)
+};
+struct StepProgram {
+  const StepPhase* ph;  // device array
+  int nph;
+  unsigned* done;       // [nph] CTAs that finished each phase, zero at launch
+  unsigned* head_cnt;   // [layers][heads] attention parts merged, zero at launch
+  float* part;          // [heads][splits][head_dim + 2] attention partials
+  int splits;           // key parts per head
+  int slot_bytes, nslots;  // the shared-memory ring
+  int rec_bytes;           // the input record area after the ring
+  int* err;
+};
+constexpr int kStepDynSmem = 208 * 1024;  // ring + input record
+constexpr int kStepRecBytes = 40 * 1024;  // largest input record (f32 k <= 10240)
+// CTAs of the step kernel on this device (one per SM), 0 if it cannot be resident.
+int step_kernel_ctas(int wtype);
+void step_kernel_init_device();
+void launch_step_kernel(const StepProgram& pg, int wtype, int ctas, cudaStream_t s);
+
 // Weight packing: f32 [n][k] (device) into the layout of wtype. interleave_half = F swaps
 // rows so that packed row 2i is source row i and 2i+1 is source row F + i (SwiGLU).
 void launch_pack_linear(const float* src, uint8_t* dst, int64_t row_stride, int n, int k,

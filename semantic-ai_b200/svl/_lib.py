@@ -45,6 +45,7 @@ SIGNATURES = {
     "svl_tts_step_device": (_I, [_P, _P, _I, _P, _P, _I, _P, _P, _P]),
     "svl_profile_kernels": (_I, [_P, _P, _I, _I, _I, _P, ctypes.POINTER(ctypes.c_int64)]),
     "svl_step_kernel_count": (_I, [_P, _P, _I, ctypes.POINTER(ctypes.c_int32)]),
+    "svl_state_error": (_I, [_P]),
     "svl_stt_head_noalloc": (_I, [_P, _I, _P, _P, _P, _P]),
     "svl_last_error": (ctypes.c_char_p, []),
     "svl_version": (ctypes.c_char_p, []),
