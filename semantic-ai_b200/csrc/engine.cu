@@ -321,6 +321,32 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
 
 void build_step_program(Model& m, State& s);
 
+// Many streams over Q8_0 / Q4_1 weights run on the tensor cores from bf16 images of the
+// dequantised matrices, built once per model when the first such state is created (the
+// packed weights stay in use for small batches). The images hold exactly the values the
+// quantised dot products use, rounded to bf16, and cost 2 bytes per weight of device memory.
+void ensure_shadows(Model& m) {
+  std::lock_guard<std::mutex> lock(m.shadow_mu);
+  if (m.shadows) return;
+  auto shadow = [&](Linear& L) {
+    if (L.wtype != W_Q8 && L.wtype != W_Q4) return;
+    const int64_t stride = packed_row_stride(W_BF16, L.k);
+    L.shadow.alloc(stride * L.n);
+    launch_dequant_bf16(L.w.as<uint8_t>(), L.row_stride, L.n, L.k, L.wtype, L.shadow.p, stride, m.stream);
+    if (!make_gemm_operand(L.tc, L.shadow.p, L.n, L.k, stride, 128))
+      throw Error(SVL_ERR_CUDA, "cannot encode the TMA tensor map of a dequantised matrix");
+  };
+  for (Layer& L : m.layers) {
+    shadow(L.in_proj);
+    shadow(L.out_proj);
+    shadow(L.ff1);
+    shadow(L.ff2);
+  }
+  if (m.kind == 0) shadow(m.text_linear);
+  check_cuda(cudaStreamSynchronize(m.stream), "dequantise");
+  m.shadows = true;
+}
+
 void queue_error_read(State& s, cudaStream_t st) {
   check_cuda(cudaMemcpyAsync(s.h_err.p, s.err.p, 4, cudaMemcpyDeviceToHost, st), "d2h");
 }
@@ -384,7 +410,9 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     if (m->kind == 0) cand = std::max<int64_t>(cand, (int64_t)max_batch * ((m->stt.text_card + 127) / 128));
     s->am_val.alloc(cand * 4);
     s->am_idx.alloc(cand * 4);
-    if (c.weight_dtype == SVL_DT_BF16 && max_batch >= kGemmMinBatch) {
+    const bool quantised = c.weight_dtype == SVL_DT_Q8_0 || c.weight_dtype == SVL_DT_Q4_1;
+    if ((c.weight_dtype == SVL_DT_BF16 || quantised) && max_batch >= kGemmMinBatch) {
+      if (quantised) ensure_shadows(*m);
       const int kx = std::max({d, qd, m->kind == 1 ? m->tts.flow_dim : 0, m->kind == 1 ? m->tts.latent_dim : 0});
       s->xa.alloc((int64_t)max_batch * kx * 2);
       s->xh.alloc((int64_t)max_batch * c.ffn_hidden * 2);
@@ -496,7 +524,7 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
                          bool do_attn);
 
 bool use_tensor_cores(const Model& m, const State& s, int nb) {
-  return m.cfg.weight_dtype == SVL_DT_BF16 && nb >= kGemmMinBatch && s.xa.p != nullptr;
+  return (m.cfg.weight_dtype == SVL_DT_BF16 || m.shadows) && nb >= kGemmMinBatch && s.xa.p != nullptr;
 }
 
 namespace {
@@ -597,6 +625,7 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
   const int* pos = s.pos.as<int>() + b0;
   const bool tc = use_tensor_cores(m, s, nb);
   const int ti = tc ? tile_index(nb) : 0;
+  const int quant = m.shadows ? 1 : 0;  // the Q8 activation blocks of a quantised model
   float2* rope_cs = tc ? s.rope_cs.as<float2>() + (int64_t)b0 * (hd / 2) : nullptr;
   if (tc && do_lin) launch_rope_table(pos, nb, m.inv_freq.as<float>(), hd / 2, rope_cs, st);
   for (int l = 0; l < c.num_layers; l++) {
@@ -606,7 +635,7 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g.rope_cs = rope_cs;
     if (do_lin && tc) {
       launch_prep_bf16(x, d, nb, L.norm1.kind, L.norm1.w.as<float>(), L.norm1.b.as<float>(),
-                       L.norm1.eps, d, s.xa.p, d, st);
+                       L.norm1.eps, d, s.xa.p, d, st, quant);
       launch_gemm(g, L.in_proj.tc, s.xa_d[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
     } else if (do_lin) {
       launch_gemv(g, st);
@@ -615,7 +644,7 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     if (!do_lin) continue;
     g = lp.out_proj;
     if (tc) {
-      launch_prep_bf16(lp.attn.out, qd, nb, NORM_NONE, nullptr, nullptr, 0.f, qd, s.xa.p, qd, st);
+      launch_prep_bf16(lp.attn.out, qd, nb, NORM_NONE, nullptr, nullptr, 0.f, qd, s.xa.p, qd, st, quant);
       launch_gemm(g, L.out_proj.tc, s.xa_q[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
     } else {
       launch_gemv(g, st);
@@ -623,9 +652,16 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g = lp.ff1;
     if (tc) {
       launch_prep_bf16(x, d, nb, L.norm2.kind, L.norm2.w.as<float>(), L.norm2.b.as<float>(),
-                       L.norm2.eps, d, s.xa.p, d, st);
-      g.out = s.xh.as<float>();  // bf16 hidden rows, the operand of linear_out
-      launch_gemm(g, L.ff1.tc, s.xa_d[ti], 0, 1, s.err.as<int>(), s.gemm_ws.as<float>(), st);
+                       L.norm2.eps, d, s.xa.p, d, st, quant);
+      if (quant) {
+        // f32 hidden rows, then their Q8 activation blocks as the operand of linear_out.
+        launch_gemm(g, L.ff1.tc, s.xa_d[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
+        launch_prep_bf16(g.out, c.ffn_hidden, nb, NORM_NONE, nullptr, nullptr, 0.f, c.ffn_hidden,
+                         s.xh.p, c.ffn_hidden, st, 1);
+      } else {
+        g.out = s.xh.as<float>();  // bf16 hidden rows, the operand of linear_out
+        launch_gemm(g, L.ff1.tc, s.xa_d[ti], 0, 1, s.err.as<int>(), s.gemm_ws.as<float>(), st);
+      }
     } else {
       launch_gemv(g, st);
     }
@@ -743,7 +779,8 @@ void launch_head(Model& m, State& s, const GemvParams& g, cudaStream_t st) {
   if (use_tensor_cores(m, s, g.nb)) {
     const int d = m.cfg.d_model;
     launch_prep_bf16(g.x, d, g.nb, m.out_norm.kind, m.out_norm.w.as<float>(),
-                     m.out_norm.b.as<float>(), m.out_norm.eps, d, s.xa.p, d, st);
+                     m.out_norm.b.as<float>(), m.out_norm.eps, d, s.xa.p, d, st,
+                     m.shadows && m.text_linear.wtype != W_F32 ? 1 : 0);
     launch_gemm(g, m.text_linear.tc, s.xa_d[tile_index(g.nb)], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
   } else {
     launch_gemv(g, st);

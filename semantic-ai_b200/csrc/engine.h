@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <map>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -58,7 +59,8 @@ struct Linear {
   int interleave = 0;
   DevBuf w;
   DevBuf bias;  // f32 [n] or empty
-  GemmOperand tc;  // TMA map of w for the tensor-core path (bf16 weights)
+  GemmOperand tc;  // TMA map of the bf16 weights for the tensor-core path
+  DevBuf shadow;   // Q8_0 / Q4_1: the bf16 image of the dequantised weights (tensor cores)
   int64_t bytes() const { return row_stride * n + (bias.p ? 4LL * n : 0); }
 };
 
@@ -108,6 +110,8 @@ struct Model {
   Linear cond_embed, input_proj, final_mod, final_linear;
   std::vector<ResBlock> res;
   int64_t weight_bytes = 0;
+  bool shadows = false;  // quantised linears have bf16 images for the tensor-core path
+  std::mutex shadow_mu;
   cudaStream_t stream = nullptr;
   ~Model();
 };

@@ -512,7 +512,8 @@ constexpr int kPrepThreads = 256;
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const float* x, int64_t x_stride,
                                                             int norm, const float* nw,
                                                             const float* nbias, float eps, int k,
-                                                            __nv_bfloat16* out, int64_t out_stride) {
+                                                            __nv_bfloat16* out, int64_t out_stride,
+                                                            int quant) {
   __shared__ float red[2][kPrepThreads / 32];
   __shared__ float stat[2];
   pdl_launch();
@@ -564,6 +565,22 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const float* x, int6
       const float w4[4] = {w.x, w.y, w.z, w.w}, b4[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
       for (int j = 0; j < 4; j++) e[j] = (e[j] - stat[0]) * stat[1] * w4[j] + b4[j];
+    }
+    if (quant) {
+      // The activation blocks of the quantised dot products (ggml Q8_0 / Q8_1, as candle's
+      // QMatMul builds them): d = amax / 127 (stored f16), q = round(x / d); the operand is
+      // q * d, the value those products multiply. A block is 8 consecutive threads.
+      // (k % 32 == 0: the threads still in this loop form whole 8-thread blocks.)
+      const unsigned act = __activemask();
+      float amax = fmaxf(fmaxf(fabsf(e[0]), fabsf(e[1])), fmaxf(fabsf(e[2]), fabsf(e[3])));
+      amax = fmaxf(amax, __shfl_xor_sync(act, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(act, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(act, amax, 4));
+      const float d = amax / 127.0f;
+      const float id = d != 0.0f ? 1.0f / d : 0.0f;
+      const float dq = f16_round(d);
+#pragma unroll
+      for (int j = 0; j < 4; j++) e[j] = dq * (float)(int)roundf(e[j] * id);
     }
     __nv_bfloat162 lo = __floats2bfloat162_rn(e[0], e[1]), hi = __floats2bfloat162_rn(e[2], e[3]);
     uint2 pk;
@@ -702,7 +719,7 @@ void launch_gemm(const GemvParams& p, const GemmOperand& w, const GemmOperand& x
 
 void launch_prep_bf16(const float* x, int64_t x_stride, int nb, int norm, const float* norm_w,
                       const float* norm_b, float eps, int k, void* out, int64_t out_stride,
-                      cudaStream_t s) {
+                      cudaStream_t s, int quant) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nb);
   cfg.blockDim = dim3(kPrepThreads);
@@ -712,8 +729,9 @@ void launch_prep_bf16(const float* x, int64_t x_stride, int nb, int norm, const 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (quant && k % 32) quant = 0;  // quantised models have k % 32 == 0
   cudaLaunchKernelEx(&cfg, prep_kernel, x, x_stride, norm, norm_w, norm_b, eps, k,
-                     static_cast<__nv_bfloat16*>(out), out_stride);
+                     static_cast<__nv_bfloat16*>(out), out_stride, quant);
 }
 
 void gemm_init_device() {

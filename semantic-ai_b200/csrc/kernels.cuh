@@ -92,10 +92,11 @@ int gemm_split(int n, int k, int nb, int bn);
 void launch_gemm(const GemvParams& p, const GemmOperand& w, const GemmOperand& x, int x_row0,
                  int out_bf16, int* err, float* ws, cudaStream_t s);
 size_t gemm_workspace_bytes();
-// The norm of each of nb rows of x (NormKind), as bf16 rows of the GEMM operand.
+// The norm of each of nb rows of x (NormKind), as bf16 rows of the GEMM operand. quant: the
+// rows first go through the Q8 activation blocks of the quantised products (quantised models).
 void launch_prep_bf16(const float* x, int64_t x_stride, int nb, int norm, const float* norm_w,
                       const float* norm_b, float eps, int k, void* out, int64_t out_stride,
-                      cudaStream_t s);
+                      cudaStream_t s, int quant = 0);
 void gemm_init_device();
 
 struct AttnParams {
@@ -167,6 +168,10 @@ void launch_step_kernel(const StepProgram& pg, int wtype, int ctas, cudaStream_t
 void launch_pack_linear(const float* src, uint8_t* dst, int64_t row_stride, int n, int k,
                         int wtype, int interleave_half, cudaStream_t s);
 void launch_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t s);
+// bf16 rows (dst_stride bytes apart) holding the dequantised values of a packed Q8_0 / Q4_1
+// matrix.
+void launch_dequant_bf16(const uint8_t* src, int64_t row_stride, int n, int k, int wtype, void* dst,
+                         int64_t dst_stride, cudaStream_t s);
 void launch_round_bf16_inplace(float* p, int64_t n, cudaStream_t s);
 
 int64_t packed_row_stride(int wtype, int k);

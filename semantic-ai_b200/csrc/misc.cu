@@ -12,20 +12,20 @@ namespace {
 // first (validated; an id past its table sets the error flag and reads row 0), then every
 // thread sums its columns over the 1 + n_q rows.
 template <bool BF16>
-__global__ void __launch_bounds__(256) embed_kernel(const EmbedParams p) {
+__global__ void __launch_bounds__(64) embed_kernel(const EmbedParams p) {
   __shared__ uint32_t toks[kMaxCodebooks + 1];
   const int b = blockIdx.x, t = threadIdx.x;
   // x is still read by the previous kernel (programmatic dependent launch).
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (t <= p.n_q) {
-    uint32_t v = t == 0 ? p.text_tok[b] : p.audio_tok[b * p.n_q + t - 1];
-    const uint32_t lim = t == 0 ? (uint32_t)p.text_card : (uint32_t)p.card;
+  for (int i = t; i <= p.n_q; i += 64) {
+    uint32_t v = i == 0 ? p.text_tok[b] : p.audio_tok[b * p.n_q + i - 1];
+    const uint32_t lim = i == 0 ? (uint32_t)p.text_card : (uint32_t)p.card;
     if (v > lim) {
       atomicExch(p.error_flag, 1);
       v = 0;
     }
-    toks[t] = v;
+    toks[i] = v;
   }
   __syncthreads();
   auto row = [&](const void* table, int64_t r, int c4) -> float4 {
@@ -37,18 +37,27 @@ __global__ void __launch_bounds__(256) embed_kernel(const EmbedParams p) {
     return reinterpret_cast<const float4*>(reinterpret_cast<const float*>(table) + r * p.d)[c4];
   };
   float* x = p.x + (int64_t)b * p.d;
-  for (int c4 = t; c4 < p.d / 4; c4 += 256) {
-    float4 acc = row(p.text_table, toks[0], c4);
-#pragma unroll 8
-    for (int c = 0; c < p.n_q; c++) {
-      const float4 e = row(p.audio_tables, (int64_t)c * (p.card + 1) + toks[c + 1], c4);
-      acc.x = acc.x + e.x;
-      acc.y = acc.y + e.y;
-      acc.z = acc.z + e.z;
-      acc.w = acc.w + e.w;
+  // Column block blockIdx.y of 64 float4; the rows' loads go out 16 at a time, the adds stay
+  // in the reference's order.
+  const int c4 = blockIdx.y * 64 + t;
+  if (c4 >= p.d / 4) return;
+  float4 acc = row(p.text_table, toks[0], c4);
+  for (int c0 = 0; c0 < p.n_q; c0 += 16) {
+    float4 e[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+      e[j] = c0 + j < p.n_q ? row(p.audio_tables, (int64_t)(c0 + j) * (p.card + 1) + toks[c0 + j + 1], c4)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      if (c0 + j >= p.n_q) break;
+      acc.x = acc.x + e[j].x;
+      acc.y = acc.y + e[j].y;
+      acc.z = acc.z + e[j].z;
+      acc.w = acc.w + e[j].w;
     }
-    reinterpret_cast<float4*>(x)[c4] = acc;
   }
+  reinterpret_cast<float4*>(x)[c4] = acc;
 }
 
 __global__ void advance_kernel(int* pos, int nb) {
@@ -100,6 +109,31 @@ __global__ void pack_kernel(const float* src, uint8_t* dst, int64_t row_stride, 
   }
 }
 
+// The bf16 image of a packed Q8_0 / Q4_1 matrix (the values the quantised dot products use:
+// q * d, or d * q + m), one warp per (row, 32-element block); rows of k bf16, dst_stride
+// bytes apart.
+__global__ void dequant_bf16_kernel(const uint8_t* src, int64_t row_stride, int n, int k, int wtype,
+                                    __nv_bfloat16* dst, int64_t dst_stride) {
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nblk = k / QBLK;
+  if (gw >= (int64_t)n * nblk) return;
+  const int r = (int)(gw / nblk), blk = (int)(gw % nblk);
+  const uint8_t* row = src + (int64_t)r * row_stride;
+  float x;
+  if (wtype == W_Q8) {
+    const float d = __half2float(reinterpret_cast<const __half*>(row + k)[blk]);
+    x = (float)reinterpret_cast<const int8_t*>(row)[blk * QBLK + lane] * d;
+  } else {
+    const uint8_t b = row[blk * 16 + (lane & 15)];
+    const int q = lane < 16 ? (b & 15) : (b >> 4);
+    const float2 dm = __half22float2(reinterpret_cast<const __half2*>(row + k / 2)[blk]);
+    x = dm.x * (float)q + dm.y;
+  }
+  reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(dst) + (int64_t)r * dst_stride)[blk * QBLK + lane] =
+      __float2bfloat16_rn(x);
+}
+
 __global__ void f32_to_bf16_kernel(const float* src, __nv_bfloat16* dst, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
@@ -116,8 +150,8 @@ __global__ void round_bf16_kernel(float* p, int64_t n) {
 
 void launch_embed(const EmbedParams& p, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.nb);
-  cfg.blockDim = dim3(256);
+  cfg.gridDim = dim3(p.nb, (p.d / 4 + 63) / 64);
+  cfg.blockDim = dim3(64);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -158,6 +192,13 @@ void launch_rope_table(const int* pos, int nb, const float* inv_freq, int half, 
 
 void launch_advance_positions(int* pos, int nb, cudaStream_t s) {
   advance_kernel<<<(nb + 255) / 256, 256, 0, s>>>(pos, nb);
+}
+
+void launch_dequant_bf16(const uint8_t* src, int64_t row_stride, int n, int k, int wtype, void* dst,
+                         int64_t dst_stride, cudaStream_t s) {
+  const int64_t warps = (int64_t)n * (k / QBLK);
+  dequant_bf16_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(
+      src, row_stride, n, k, wtype, static_cast<__nv_bfloat16*>(dst), dst_stride);
 }
 
 int64_t packed_row_stride(int wtype, int k) {

@@ -6,9 +6,11 @@ teacher-forced with the oracle's tokens, at the bf16 bar of the north star: logi
 2e-2 relative (||diff||_2 / ||oracle||_2) per stream and step, and an argmax that may differ
 from the oracle's only where the oracle's top-2 margin is within twice the logit deviation.
 
-The shapes cover the kernel's variants: stream tiles of 64, 128 and 256 (and two stream tiles
-above 256), K split over thread-block clusters of 2 to 8 CTAs (the mid-size model's out_proj
-and linear_out), ring wrap-around, and staggered stream positions.
+Q8_0 / Q4_1 models run the same kernel on bf16 images of their dequantised weights.
+
+The shapes cover the kernel's variants: one to three 128-stream tiles (16 to 260 streams), K
+split over thread-block clusters of up to 8 CTAs (the mid-size model's out_proj and
+linear_out), ring wrap-around, and staggered stream positions.
 """
 import numpy as np
 import pytest
@@ -28,11 +30,11 @@ def mid_model():
                           card=64, n_q=4)
 
 
-def run_batch(stt, B, frames, stagger=0):
+def run_batch(stt, B, frames, stagger=0, wdt="bf16", kvdt="bf16", strict=True, envelope=None):
     """B streams step together for `frames` frames; stream b first runs b % (stagger + 1)
     frames alone (matrix-vector path, one stream) and is copied into the batch state, so the
     streams sit at different positions. Returns (worst relative diff, argmax flips)."""
-    cfg = stt.transformer("bf16", "bf16")
+    cfg = stt.transformer(wdt, kvdt)
     w = synth.stt_weights(stt, cfg)
     om = O.OracleModel(0, cfg, w, stt=stt)
     gm = LanguageModel(stt, cfg, w)
@@ -57,7 +59,18 @@ def run_batch(stt, B, frames, stagger=0):
             one.close()
     prev = np.array([stt.text_card if offsets[b] == 0 else refs[b][0][offsets[b] - 1]
                      for b in range(B)], np.uint32)
-    worst, flips = 0.0, 0
+    worst, flips, rels, env = 0.0, 0, [], []
+    if envelope is not None:
+        # The oracle against itself with the RMS-norm sum reversed, teacher-forced on its own
+        # tokens: how far a 1-ulp reduction-order change moves these logits.
+        envelope.orc_set_reduction_variant(1)
+        try:
+            for b in range(B):
+                _, alt = O.greedy_stt(om, audio[:, b], offsets[b] + frames, teacher=refs[b][0])
+                env += [float(np.linalg.norm(alt[i] - refs[b][1][i]) / np.linalg.norm(refs[b][1][i]))
+                        for i in range(offsets[b], offsets[b] + frames)]
+        finally:
+            envelope.orc_set_reduction_variant(0)
     for j in range(frames):
         a = np.stack([audio_at(b, offsets[b] + j) for b in range(B)])
         tok, lg = gm.step(prev, a, st, logits=True)
@@ -67,8 +80,9 @@ def run_batch(stt, B, frames, stagger=0):
             rel = float(np.linalg.norm(lg[b] - rl[i]) / np.linalg.norm(rl[i]))
             diff = float(np.max(np.abs(lg[b] - rl[i])))
             worst = max(worst, rel)
-            assert rel <= REL_TOL, f"stream {b} step {i}: relative logit diff {rel:.3g}"
-            if tok[b] != rt[i]:
+            rels.append(rel)
+            assert not strict or rel <= REL_TOL, f"stream {b} step {i}: relative logit diff {rel:.3g}"
+            if strict and tok[b] != rt[i]:
                 s = np.sort(rl[i])
                 assert s[-1] - s[-2] <= 2 * diff, (
                     f"stream {b} step {i}: token {tok[b]} != oracle {rt[i]} "
@@ -77,6 +91,12 @@ def run_batch(stt, B, frames, stagger=0):
             prev[b] = rt[i]
     for b in range(B):
         assert st.position(b) == offsets[b] + frames
+    if envelope is not None:
+        rels, env = np.array(rels), np.array(env)
+        print(f"  GPU vs oracle L2-rel median {np.median(rels):.3g} max {rels.max():.3g}; "
+              f"oracle self-envelope median {np.median(env):.3g} max {env.max():.3g}")
+        assert np.median(rels) <= 2 * np.median(env) + 1e-3
+        assert rels.max() <= 2 * env.max() + 1e-3
     return worst, flips
 
 
@@ -92,6 +112,18 @@ def test_mid_bf16_split_k(svl_lib, oracle_lib, B):
     stt = mid_model()
     worst, flips = run_batch(stt, B, frames=5, stagger=3)
     print(f"mid bf16 B={B}: worst relative logit diff {worst:.3g}, {flips} argmax flips")
+
+
+@pytest.mark.parametrize("wdt,kvdt", [("q8_0", "f32"), ("q4_1", "bf16")])
+def test_quantised_many_streams(svl_lib, oracle_lib, wdt, kvdt):
+    """Q8_0 / Q4_1 weights at 16+ streams: the products run on the tensor cores from bf16
+    images of the dequantised weights, against activations put through the same Q8 blocks
+    (q * d, rounded to bf16). The activation rounding is discontinuous, so as for the batch-1
+    STT-1b test the bar is the oracle's self-envelope: the GPU's median and worst L2-relative
+    deviation within twice the oracle's own under a reversed RMS-norm sum."""
+    worst, flips = run_batch(mid_model(), 40, frames=5, stagger=3, wdt=wdt, kvdt=kvdt,
+                             strict=False, envelope=oracle_lib)
+    print(f"mid {wdt} B=40: worst relative logit diff {worst:.3g}, {flips} argmax flips")
 
 
 def test_tensor_core_path_is_deterministic(svl_lib):
