@@ -321,10 +321,12 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
 
 void build_step_program(Model& m, State& s);
 
-// Many streams over Q8_0 / Q4_1 weights run on the tensor cores from bf16 images of the
+// Many streams over Q8_0 / Q4_1 weights run on the tensor cores from f16 images of the
 // dequantised matrices, built once per model when the first such state is created (the
-// packed weights stay in use for small batches). The images hold exactly the values the
-// quantised dot products use, rounded to bf16, and cost 2 bytes per weight of device memory.
+// packed weights stay in use for small batches). The images hold the values the quantised
+// dot products use (q * d, or d * q + m) rounded to f16 (11 significant bits: the products
+// of a 7-bit integer and an f16 scale lose at most 2^-12), and cost 2 bytes per weight of
+// device memory. The activations meet them as f16 values of their Q8 blocks.
 void ensure_shadows(Model& m) {
   std::lock_guard<std::mutex> lock(m.shadow_mu);
   if (m.shadows) return;
@@ -332,8 +334,8 @@ void ensure_shadows(Model& m) {
     if (L.wtype != W_Q8 && L.wtype != W_Q4) return;
     const int64_t stride = packed_row_stride(W_BF16, L.k);
     L.shadow.alloc(stride * L.n);
-    launch_dequant_bf16(L.w.as<uint8_t>(), L.row_stride, L.n, L.k, L.wtype, L.shadow.p, stride, m.stream);
-    if (!make_gemm_operand(L.tc, L.shadow.p, L.n, L.k, stride, 128))
+    launch_dequant_bf16(L.w.as<uint8_t>(), L.row_stride, L.n, L.k, L.wtype, L.shadow.p, stride, m.stream, 1);
+    if (!make_gemm_operand(L.tc, L.shadow.p, L.n, L.k, stride, 128, 1))
       throw Error(SVL_ERR_CUDA, "cannot encode the TMA tensor map of a dequantised matrix");
   };
   for (Layer& L : m.layers) {
@@ -422,10 +424,11 @@ State* create_state(Model* m, int max_batch, int max_positions) {
       s->gemm_ws.alloc(gemm_workspace_bytes());
       const int bns[3] = {64, 128, 256};
       for (int i = 0; i < 3; i++) {
-        bool ok = make_gemm_operand(s->xa_d[i], s->xa.p, max_batch, d, (int64_t)d * 2, bns[i]) &&
-                  make_gemm_operand(s->xa_q[i], s->xa.p, max_batch, qd, (int64_t)qd * 2, bns[i]) &&
+        const int f16 = quantised ? 1 : 0;
+        bool ok = make_gemm_operand(s->xa_d[i], s->xa.p, max_batch, d, (int64_t)d * 2, bns[i], f16) &&
+                  make_gemm_operand(s->xa_q[i], s->xa.p, max_batch, qd, (int64_t)qd * 2, bns[i], f16) &&
                   make_gemm_operand(s->xh_f[i], s->xh.p, max_batch, c.ffn_hidden,
-                                    (int64_t)c.ffn_hidden * 2, bns[i]);
+                                    (int64_t)c.ffn_hidden * 2, bns[i], f16);
         if (!ok) throw Error(SVL_ERR_CUDA, "cannot encode the TMA tensor maps of the GEMM operands");
       }
     }
@@ -635,7 +638,7 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g.rope_cs = rope_cs;
     if (do_lin && tc) {
       launch_prep_bf16(x, d, nb, L.norm1.kind, L.norm1.w.as<float>(), L.norm1.b.as<float>(),
-                       L.norm1.eps, d, s.xa.p, d, st, quant);
+                       L.norm1.eps, d, s.xa.p, d, st, quant, quant);
       launch_gemm(g, L.in_proj.tc, s.xa_d[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
     } else if (do_lin) {
       launch_gemv(g, st);
@@ -644,7 +647,7 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     if (!do_lin) continue;
     g = lp.out_proj;
     if (tc) {
-      launch_prep_bf16(lp.attn.out, qd, nb, NORM_NONE, nullptr, nullptr, 0.f, qd, s.xa.p, qd, st, quant);
+      launch_prep_bf16(lp.attn.out, qd, nb, NORM_NONE, nullptr, nullptr, 0.f, qd, s.xa.p, qd, st, quant, quant);
       launch_gemm(g, L.out_proj.tc, s.xa_q[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
     } else {
       launch_gemv(g, st);
@@ -652,12 +655,12 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     g = lp.ff1;
     if (tc) {
       launch_prep_bf16(x, d, nb, L.norm2.kind, L.norm2.w.as<float>(), L.norm2.b.as<float>(),
-                       L.norm2.eps, d, s.xa.p, d, st, quant);
+                       L.norm2.eps, d, s.xa.p, d, st, quant, quant);
       if (quant) {
         // f32 hidden rows, then their Q8 activation blocks as the operand of linear_out.
         launch_gemm(g, L.ff1.tc, s.xa_d[ti], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
         launch_prep_bf16(g.out, c.ffn_hidden, nb, NORM_NONE, nullptr, nullptr, 0.f, c.ffn_hidden,
-                         s.xh.p, c.ffn_hidden, st, 1);
+                         s.xh.p, c.ffn_hidden, st, 1, 1);
       } else {
         g.out = s.xh.as<float>();  // bf16 hidden rows, the operand of linear_out
         launch_gemm(g, L.ff1.tc, s.xa_d[ti], 0, 1, s.err.as<int>(), s.gemm_ws.as<float>(), st);
@@ -780,7 +783,7 @@ void launch_head(Model& m, State& s, const GemvParams& g, cudaStream_t st) {
     const int d = m.cfg.d_model;
     launch_prep_bf16(g.x, d, g.nb, m.out_norm.kind, m.out_norm.w.as<float>(),
                      m.out_norm.b.as<float>(), m.out_norm.eps, d, s.xa.p, d, st,
-                     m.shadows && m.text_linear.wtype != W_F32 ? 1 : 0);
+                     m.shadows ? 1 : 0, m.shadows ? 1 : 0);
     launch_gemm(g, m.text_linear.tc, s.xa_d[tile_index(g.nb)], 0, 0, s.err.as<int>(), s.gemm_ws.as<float>(), st);
   } else {
     launch_gemv(g, st);

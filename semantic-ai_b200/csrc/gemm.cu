@@ -58,9 +58,10 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
          (2ull << 61);
 }
-// Instruction descriptor of kind::f16: f32 accumulator, bf16 A and B, both K-major.
-__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+// Instruction descriptor of kind::f16: f32 accumulator, A and B both bf16 (fmt 1) or both
+// f16 (fmt 0), both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16kind(int m, int n, uint32_t fmt) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) |
          ((uint32_t)(m >> 4) << 24);
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int c0, int c1,
@@ -262,6 +263,7 @@ struct GemmArgs {
   int out_bf16;      // STORE / SWIGLU / GELU / SILU outputs as bf16
   int* err;          // set when a bounded wait runs out
   float* ws;         // split exchange: [CTA][BN streams][128 rows] f32 partial tiles
+  uint32_t idesc;    // instruction descriptor (operand type)
 };
 
 
@@ -344,7 +346,7 @@ __global__ void __launch_bounds__(kGThreads, Cfg<BN>::kMinBlocks)
     }
   } else if (warp == 1 && lane == 0) {
     // MMA issuer.
-    constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+    const uint32_t idesc = ga.idesc;
     for (int i = 0; i < nkb; i++) {
       const int st = i % C::kStages;
       if (!mbar_wait(&full_bar[st], (i / C::kStages) & 1)) {
@@ -512,15 +514,15 @@ constexpr int kPrepThreads = 256;
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const float* x, int64_t x_stride,
                                                             int norm, const float* nw,
                                                             const float* nbias, float eps, int k,
-                                                            __nv_bfloat16* out, int64_t out_stride,
-                                                            int quant) {
+                                                            uint16_t* out, int64_t out_stride,
+                                                            int quant, int f16) {
   __shared__ float red[2][kPrepThreads / 32];
   __shared__ float stat[2];
   pdl_launch();
   pdl_wait();
   const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const float* xr = x + b * x_stride;
-  __nv_bfloat16* o = out + b * out_stride;
+  uint16_t* o = out + b * out_stride;
   if (norm != NORM_NONE) {
     float s = 0.f, s2 = 0.f;
     for (int i = t * 4; i < k; i += kPrepThreads * 4) {
@@ -582,10 +584,16 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const float* x, int6
 #pragma unroll
       for (int j = 0; j < 4; j++) e[j] = dq * (float)(int)roundf(e[j] * id);
     }
-    __nv_bfloat162 lo = __floats2bfloat162_rn(e[0], e[1]), hi = __floats2bfloat162_rn(e[2], e[3]);
     uint2 pk;
-    pk.x = *reinterpret_cast<uint32_t*>(&lo);
-    pk.y = *reinterpret_cast<uint32_t*>(&hi);
+    if (f16) {
+      __half2 lo = __floats2half2_rn(e[0], e[1]), hi = __floats2half2_rn(e[2], e[3]);
+      pk.x = *reinterpret_cast<uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<uint32_t*>(&hi);
+    } else {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(e[0], e[1]), hi = __floats2bfloat162_rn(e[2], e[3]);
+      pk.x = *reinterpret_cast<uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<uint32_t*>(&hi);
+    }
     *reinterpret_cast<uint2*>(o + i) = pk;
   }
 }
@@ -661,7 +669,7 @@ void set_attrs_bn() {
 }  // namespace
 
 bool make_gemm_operand(GemmOperand& op, const void* base, int rows, int k, int64_t row_bytes,
-                       int box_rows) {
+                       int box_rows, int f16) {
   static_assert(sizeof(op.map) >= sizeof(CUtensorMap), "tensor map storage");
   EncodeTiled enc = encoder();
   if (!enc || !base || rows <= 0 || k <= 0 || row_bytes % 16 || box_rows > 256 || box_rows < 8 ||
@@ -671,13 +679,15 @@ bool make_gemm_operand(GemmOperand& op, const void* base, int rows, int k, int64
   const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
   const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(reinterpret_cast<CUtensorMap*>(op.map), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+  CUresult r = enc(reinterpret_cast<CUtensorMap*>(op.map),
+                   f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   op.rows = rows;
   op.k = k;
   op.box_rows = box_rows;
+  op.f16 = f16;
   op.valid = r == CUDA_SUCCESS;
   return op.valid;
 }
@@ -708,6 +718,8 @@ void launch_gemm(const GemvParams& p, const GemmOperand& w, const GemmOperand& x
   ga.out_bf16 = out_bf16;
   ga.err = err;
   ga.ws = ws;
+  ga.idesc = idesc_f16kind(kBM, x.box_rows, w.f16 ? 0u : 1u);
+  if (w.f16 != x.f16) return;  // mixed operand types are not an MMA kind::f16 form
   const int bn = x.box_rows;
   const int tiles = (p.n + kBM - 1) / kBM;
   const int stream_tiles = (p.nb + bn - 1) / bn;
@@ -719,7 +731,7 @@ void launch_gemm(const GemvParams& p, const GemmOperand& w, const GemmOperand& x
 
 void launch_prep_bf16(const float* x, int64_t x_stride, int nb, int norm, const float* norm_w,
                       const float* norm_b, float eps, int k, void* out, int64_t out_stride,
-                      cudaStream_t s, int quant) {
+                      cudaStream_t s, int quant, int f16) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nb);
   cfg.blockDim = dim3(kPrepThreads);
@@ -731,7 +743,7 @@ void launch_prep_bf16(const float* x, int64_t x_stride, int nb, int norm, const 
   cfg.numAttrs = 1;
   if (quant && k % 32) quant = 0;  // quantised models have k % 32 == 0
   cudaLaunchKernelEx(&cfg, prep_kernel, x, x_stride, norm, norm_w, norm_b, eps, k,
-                     static_cast<__nv_bfloat16*>(out), out_stride, quant);
+                     static_cast<uint16_t*>(out), out_stride, quant, f16);
 }
 
 void gemm_init_device() {

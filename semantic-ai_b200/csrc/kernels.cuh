@@ -77,10 +77,11 @@ void gemv_init_device();
 struct GemmOperand {
   alignas(64) unsigned char map[128];  // CUtensorMap
   int rows = 0, k = 0, box_rows = 0;
+  int f16 = 0;  // element type: 0 bf16, 1 f16 (both operands of a product share it)
   bool valid = false;
 };
 bool make_gemm_operand(GemmOperand& op, const void* base, int rows, int k, int64_t row_bytes,
-                       int box_rows);
+                       int box_rows, int f16 = 0);
 // Streams per GEMM tile (the MMA's N, and the box height of the X operand) for nb streams.
 int gemm_stream_tile(int nb);
 // Cluster split of K for an n x k product over nb streams with stream tiles of bn.
@@ -92,11 +93,13 @@ int gemm_split(int n, int k, int nb, int bn);
 void launch_gemm(const GemvParams& p, const GemmOperand& w, const GemmOperand& x, int x_row0,
                  int out_bf16, int* err, float* ws, cudaStream_t s);
 size_t gemm_workspace_bytes();
-// The norm of each of nb rows of x (NormKind), as bf16 rows of the GEMM operand. quant: the
-// rows first go through the Q8 activation blocks of the quantised products (quantised models).
+// The norm of each of nb rows of x (NormKind), as bf16 (or f16) rows of the GEMM operand.
+// quant: the rows first go through the Q8 activation blocks of the quantised products
+// (quantised models, whose operands are f16).
 void launch_prep_bf16(const float* x, int64_t x_stride, int nb, int norm, const float* norm_w,
                       const float* norm_b, float eps, int k, void* out, int64_t out_stride,
-                      cudaStream_t s, int quant = 0);
+                      cudaStream_t s, int quant = 0, int f16 = 0);
+// bf16 / f16 images of dequantised weights (launch_dequant_bf16 with f16 = 1 writes f16).
 void gemm_init_device();
 
 struct AttnParams {
@@ -171,7 +174,7 @@ void launch_f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t s);
 // bf16 rows (dst_stride bytes apart) holding the dequantised values of a packed Q8_0 / Q4_1
 // matrix.
 void launch_dequant_bf16(const uint8_t* src, int64_t row_stride, int n, int k, int wtype, void* dst,
-                         int64_t dst_stride, cudaStream_t s);
+                         int64_t dst_stride, cudaStream_t s, int f16 = 0);
 void launch_round_bf16_inplace(float* p, int64_t n, cudaStream_t s);
 
 int64_t packed_row_stride(int wtype, int k);

@@ -113,7 +113,7 @@ __global__ void pack_kernel(const float* src, uint8_t* dst, int64_t row_stride, 
 // q * d, or d * q + m), one warp per (row, 32-element block); rows of k bf16, dst_stride
 // bytes apart.
 __global__ void dequant_bf16_kernel(const uint8_t* src, int64_t row_stride, int n, int k, int wtype,
-                                    __nv_bfloat16* dst, int64_t dst_stride) {
+                                    uint16_t* dst, int64_t dst_stride, int f16) {
   const int lane = threadIdx.x & 31;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nblk = k / QBLK;
@@ -130,8 +130,14 @@ __global__ void dequant_bf16_kernel(const uint8_t* src, int64_t row_stride, int 
     const float2 dm = __half22float2(reinterpret_cast<const __half2*>(row + k / 2)[blk]);
     x = dm.x * (float)q + dm.y;
   }
-  reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(dst) + (int64_t)r * dst_stride)[blk * QBLK + lane] =
-      __float2bfloat16_rn(x);
+  uint16_t* o = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(dst) + (int64_t)r * dst_stride);
+  if (f16) {
+    const __half h = __float2half_rn(x);
+    o[blk * QBLK + lane] = *reinterpret_cast<const uint16_t*>(&h);
+  } else {
+    const __nv_bfloat16 h = __float2bfloat16_rn(x);
+    o[blk * QBLK + lane] = *reinterpret_cast<const uint16_t*>(&h);
+  }
 }
 
 __global__ void f32_to_bf16_kernel(const float* src, __nv_bfloat16* dst, int64_t n) {
@@ -195,10 +201,10 @@ void launch_advance_positions(int* pos, int nb, cudaStream_t s) {
 }
 
 void launch_dequant_bf16(const uint8_t* src, int64_t row_stride, int n, int k, int wtype, void* dst,
-                         int64_t dst_stride, cudaStream_t s) {
+                         int64_t dst_stride, cudaStream_t s, int f16) {
   const int64_t warps = (int64_t)n * (k / QBLK);
   dequant_bf16_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(
-      src, row_stride, n, k, wtype, static_cast<__nv_bfloat16*>(dst), dst_stride);
+      src, row_stride, n, k, wtype, static_cast<uint16_t*>(dst), dst_stride, f16);
 }
 
 int64_t packed_row_stride(int wtype, int k) {
