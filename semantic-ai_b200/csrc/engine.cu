@@ -406,6 +406,18 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     int splits = (148 + units - 1) / units;
     splits = std::max(1, std::min({splits, (s->cap + 15) / 16, attention_max_splits()}));
     s->splits = splits;
+    if (splits == 1) {
+      // Many streams: pieces of keys spread over the warps, partials merged per unit.
+      s->piece = attention_piece(c.head_dim, s->kv_elt == 2, s->cap, &s->npieces);
+      s->attn_part.alloc((int64_t)units * s->npieces * (c.head_dim + 4) * 4);
+      if (s->kv_elt == 2) {
+        const int64_t rows = (int64_t)max_batch * c.num_kv_heads * s->cap;
+        const int box = attention_chunk_keys(c.head_dim, 1);
+        s->ring_maps = rows < (int64_t)1 << 31 &&
+                       make_ring_map(s->kmap, s->k_ring.p, rows, c.head_dim, c.num_layers, s->ring_layer_stride, box) &&
+                       make_ring_map(s->vmap, s->v_ring.p, rows, c.head_dim, c.num_layers, s->ring_layer_stride, box);
+      }
+    }
     // Argmax candidates: [stream][CTA] of the matrix-vector head, [stream][row tile] of the
     // tensor-core head.
     int64_t cand = kMaxNbChunk * kLogitsGrid;
@@ -591,6 +603,13 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   a.window = c.context;
   a.scale = std::pow((float)hd, -0.5f);
   a.splits = s.splits;
+  a.piece = s.piece;
+  a.npieces = s.npieces;
+  a.part = s.attn_part.as<float>();
+  a.kmap = s.ring_maps ? s.kmap : nullptr;
+  a.vmap = s.ring_maps ? s.vmap : nullptr;
+  a.layer = l;
+  a.ring_row0 = b0 * c.num_kv_heads * s.cap;
   a.out = attn;
   a.err = s.err.as<int>();
   // out_proj + residual (nn/transformer.rs:344, :239-243).

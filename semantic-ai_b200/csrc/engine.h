@@ -136,6 +136,12 @@ struct State {
   std::map<int64_t, GemmOperand> xa_by_k;  // bf16 operand maps over xa, keyed by k * 512 + bn
   HostBuf h_tok_in, h_audio_in, h_tok_out, h_err;
   int splits = 1;
+  // Many-stream attention (splits == 1): keys per piece, pieces per unit at most, and the
+  // partials of the units of several pieces.
+  int piece = 0, npieces = 0;
+  DevBuf attn_part;
+  alignas(64) unsigned char kmap[128], vmap[128];  // bf16 rings as TMA tensors
+  bool ring_maps = false;
   // Tensor-core path (bf16 weights, many streams): bf16 operand rows and their TMA maps, per
   // stream-tile width (64, 128, 256). xa holds normalised inputs / attention outputs, xh the
   // feed-forward hidden rows.

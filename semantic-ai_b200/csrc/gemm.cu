@@ -692,6 +692,22 @@ bool make_gemm_operand(GemmOperand& op, const void* base, int rows, int k, int64
   return op.valid;
 }
 
+bool make_ring_map(unsigned char* map128, const void* base, int64_t rows, int head_dim, int layers,
+                   int64_t layer_stride, int box_rows) {
+  EncodeTiled enc = encoder();
+  if (!enc || !base || rows <= 0 || head_dim % 64 || layers <= 0 || (layer_stride * 2) % 16 ||
+      box_rows > 256 || box_rows < 1 || reinterpret_cast<uintptr_t>(base) % 16)
+    return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)rows, (cuuint64_t)layers};
+  const cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, (cuuint64_t)layer_stride * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(reinterpret_cast<CUtensorMap*>(map128), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int gemm_stream_tile(int nb) { return nb > 0 ? 128 : 128; }
 
 int gemm_split(int n, int k, int nb, int bn) {

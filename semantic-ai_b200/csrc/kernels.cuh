@@ -82,6 +82,12 @@ struct GemmOperand {
 };
 bool make_gemm_operand(GemmOperand& op, const void* base, int rows, int k, int64_t row_bytes,
                        int box_rows, int f16 = 0);
+// A bf16 KV ring as a 3-D tensor [layers][rows][head_dim] (rows = streams x kv_heads x slots,
+// layer_stride elements apart) for TMA boxes of 64 dims x box_rows rows, 128-byte swizzle.
+bool make_ring_map(unsigned char* map128, const void* base, int64_t rows, int head_dim, int layers,
+                   int64_t layer_stride, int box_rows);
+// Keys per chunk of the many-stream attention (the box height of its ring maps).
+int attention_chunk_keys(int head_dim, int kv_bf16);
 // Streams per GEMM tile (the MMA's N, and the box height of the X operand) for nb streams.
 int gemm_stream_tile(int nb);
 // Cluster split of K for an n x k product over nb streams with stream tiles of bn.
@@ -113,11 +119,23 @@ struct AttnParams {
   float scale;
   int splits;            // key chunks per (stream, head): one thread-block cluster
   float* out;            // [nb][heads * head_dim]
-  int* err;              // set to 1 when a bounded wait runs out
+  int* err;              // set to 4 when a bounded wait runs out
+  // Many streams (splits == 1): keys per piece, pieces per unit at most, and the partials
+  // [nb][heads][npieces][head_dim + 4] of the units of several pieces.
+  int piece, npieces;
+  float* part;
+  // Tensor-map view of bf16 rings (make_ring_map): host copies of the maps of k_ring's and
+  // v_ring's whole allocations, this layer's index in them, and the map row of stream 0's slot 0.
+  const unsigned char* kmap;
+  const unsigned char* vmap;
+  int layer, ring_row0;
 };
 
 void launch_attention_decode(const AttnParams& p, cudaStream_t s);
 int attention_max_splits();
+// Keys per piece of the many-stream attention for a ring of `ring_cap` keys; *npieces = the
+// most pieces a (stream, head) can have.
+int attention_piece(int head_dim, int kv_bf16, int ring_cap, int* npieces);
 // Per device, once: raises the dynamic shared-memory limit of the attention kernels.
 void attention_init_device();
 
