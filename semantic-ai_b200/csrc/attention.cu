@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const AttnParams p) {
 //
 // The warp is its own producer. bf16 caches: lane 0 loads a chunk's keys and values with
 // tensor-map copies (boxes of 64 dims x KC slots, 128-byte swizzle, so ldmatrix reads them
-// without bank conflicts) into the warp's 3-slot ring, and the item's q with its first chunk;
+// without bank conflicts) into the warp's 2-slot ring, and the item's q with its first chunk;
 // q.k and p.v run on the tensor cores (mma m16n8k16, f32 accumulation). The f32 operand (q,
 // then the probabilities) is split into three bf16 parts x = hi + mid + lo (24 significant
 // bits, the f32 value to rounding) placed in rows 0, 8 and 1 of the A tile, so a key's score
@@ -322,9 +322,9 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const AttnParams p) {
 // A unit of one piece writes its output directly; otherwise each piece writes its partial
 // (max, sum, weighted values) and attn_merge_kernel, launched next, combines them in piece
 // order. Every wait is bounded (a wait that runs out sets *p.err to 4).
-constexpr int kWWarps = 8;                 // warps per CTA
-constexpr int kWSlots = 3;                 // ring slots per warp
-constexpr int kWQueue = 4;                 // item descriptors in flight per warp (3 chunks ahead)
+constexpr int kWWarps = 12;                // warps per CTA (one CTA per SM)
+constexpr int kWSlots = 2;                 // ring slots per warp
+constexpr int kWQueue = 4;                 // item descriptors in flight per warp (> slots)
 constexpr int kMergeWarps = 8;             // attn_merge_kernel: one warp per unit
 constexpr int kWMaxPieces = 16;
 constexpr int kWChunk = 8192;              // keys and values of a chunk
