@@ -4,15 +4,15 @@
 // same products on the CPU through kernels::matvec, nn/kernels/matvec.rs:29-58, and
 // candle's QMatMul, nn/mod.rs:97). Each warp owns a contiguous range of row groups (R rows)
 // and streams them straight from global memory into registers, 16 bytes per lane and U
-// loads per row in flight, with 2 CTAs of 8 warps per SM, so about 64 KB per SM is in
-// flight. With programmatic dependent launch, each warp issues its first group's loads
-// before griddepcontrol.wait (weights do not depend on the previous kernel), and one thread
-// per CTA pulls its share of a later kernel's weights into L2 (cp.async.bulk.prefetch.L2).
-// After the wait, every CTA turns the input row(s) into records in shared memory -- the
-// layer's norm (candle rms_norm / layer_norm) and the conversion for the weight format
-// (bf16 rounding, or the Q8_0 / Q8_1 activation blocks candle's QMatMul builds) -- while
-// those first weight loads are still in flight. Each row group ends with the fused epilogue
-// (RoPE + KV-ring write, SwiGLU, GELU, SiLU, residual add, logits + argmax).
+// loads per row in flight (with the block formats' scales), with 2 CTAs of 8 warps per SM.
+// With programmatic dependent launch, each warp issues its first group's loads before
+// griddepcontrol.wait (weights do not depend on the previous kernel), and one thread per CTA
+// pulls its share of a later kernel's weights into L2 (cp.async.bulk.prefetch.L2). After the
+// wait, every CTA turns the input row(s) into records in shared memory -- the layer's norm
+// (candle rms_norm / layer_norm) and the conversion for the weight format (bf16 rounding, or
+// the Q8_0 / Q8_1 activation blocks candle's QMatMul builds) -- while those first weight
+// loads are still in flight. Each row group ends with the fused epilogue (RoPE + KV-ring
+// write, SwiGLU, GELU, SiLU, residual add, logits + argmax), one lane per (row, stream).
 #include "common.cuh"
 #include "gemv_common.cuh"
 #include "kernels.cuh"
@@ -35,17 +35,19 @@ __device__ __forceinline__ uint4 ldg_weights(const void* p) {
                : "l"(p));
   return r;
 }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// Accumulates chunks [c0, c0 + 32 U) of R rows (weights already in wv) against the NB input
-// records in shared memory (record b at xsm + b * rec: see input_rec_bytes).
+// Accumulates chunks [c0, c0 + 32 U) of R rows (weights already in wv, and for the block
+// formats their scales in ws) against the NB input records in shared memory (record b at
+// xsm + b * rec: see input_rec_bytes).
 template <int WT, int NB, int R, int U>
-__device__ __forceinline__ void dot_chunks(const uint4 (&wv)[R][U], const GemvParams& p, int g, int c0,
-                                           const uint8_t* xsm, int rec, int lane, float (&acc)[R][NB]) {
+__device__ __forceinline__ void dot_chunks(const uint4 (&wv)[R][U], const uint32_t (&ws)[R][U],
+                                           const GemvParams& p, int g, int c0, const uint8_t* xsm,
+                                           int rec, int lane, float (&acc)[R][NB]) {
   const int k = p.k, nch = chunks_per_row(WT, k), nblk = k / QBLK;
 #pragma unroll
   for (int u = 0; u < U; u++) {
@@ -95,10 +97,7 @@ __device__ __forceinline__ void dot_chunks(const uint4 (&wv)[R][U], const GemvPa
       const int blk = c >> 1;
       float dw[R];
 #pragma unroll
-      for (int r = 0; r < R; r++) {
-        const int row = g * R + r;
-        dw[r] = (valid && row < p.n) ? __half2float(reinterpret_cast<const __half*>(p.w + (int64_t)row * p.row_stride + k)[blk]) : 0.f;
-      }
+      for (int r = 0; r < R; r++) dw[r] = __half2float(__ushort_as_half((unsigned short)ws[r][u]));
 #pragma unroll
       for (int b = 0; b < NB; b++) {
         const uint8_t* xr = xsm + (size_t)b * rec;
@@ -120,9 +119,8 @@ __device__ __forceinline__ void dot_chunks(const uint4 (&wv)[R][U], const GemvPa
         float2 dm[R];
 #pragma unroll
         for (int r = 0; r < R; r++) {
-          const int row = g * R + r;
-          dm[r] = row < p.n ? __half22float2(reinterpret_cast<const __half2*>(p.w + (int64_t)row * p.row_stride + k / 2)[c])
-                            : make_float2(0.f, 0.f);
+          const uint32_t h = ws[r][u];
+          dm[r] = __half22float2(*reinterpret_cast<const __half2*>(&h));
         }
 #pragma unroll
         for (int b = 0; b < NB; b++) {
@@ -169,6 +167,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
   const int g0 = (int)((int64_t)gw * groups / total_w), g1 = (int)((int64_t)(gw + 1) * groups / total_w);
 
   uint4 wv[R][U];
+  uint32_t ws[R][U];  // block formats: the scale (q8_0: d) or scale and min (q4_1) of each chunk
+  // Loads chunks [c0, c0 + 32 U) of group g's rows, with their block scales: every load of
+  // the group is in flight at once.
   auto issue = [&](int g, int c0) {
 #pragma unroll
     for (int r = 0; r < R; r++)
@@ -176,9 +177,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
       for (int u = 0; u < U; u++) {
         const int c = c0 + lane + 32 * u;
         const int row = g * R + r;
-        wv[r][u] = (g < g1 && c < nch && row < p.n)
-                       ? ldg_weights(p.w + (int64_t)row * p.row_stride + (int64_t)c * 16)
-                       : make_uint4(0, 0, 0, 0);
+        const bool on = g < g1 && c < nch && row < p.n;
+        const uint8_t* wrow = p.w + (int64_t)row * p.row_stride;
+        wv[r][u] = on ? ldg_weights(wrow + (int64_t)c * 16) : make_uint4(0, 0, 0, 0);
+        ws[r][u] = 0u;
+        if (WT == W_Q8 && on)
+          ws[r][u] = reinterpret_cast<const unsigned short*>(wrow + p.k)[c >> 1];
+        else if (WT == W_Q4 && on)
+          ws[r][u] = reinterpret_cast<const uint32_t*>(wrow + p.k / 2)[c];
       }
   };
   // Weights do not depend on the previous kernel: first group's loads and the L2 prefetch
@@ -204,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
       for (int b = 0; b < NB; b++) acc[r][b] = 0.f;
     for (int c0 = 0; c0 < nch; c0 += 32 * U) {
       if (c0 > 0) issue(g, c0);
-      dot_chunks<WT, NB, R, U>(wv, p, g, c0, xsm, rec, lane, acc);
+      dot_chunks<WT, NB, R, U>(wv, ws, p, g, c0, xsm, rec, lane, acc);
     }
     // The next group's first loads fly while this group reduces and runs its epilogue.
     if (g + 1 < g1) issue(g + 1, 0);
@@ -229,11 +235,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
         }
       }
     }
+    // Lane j < R NB runs the epilogue of (row + j / NB, stream j % NB); all at once.
+    {
+      float v = 0.f, v_lo = 0.f, v_hi = 0.f;
 #pragma unroll
-    for (int jj = 0; jj < R * NB; jj++) {
-      const int r = jj / NB, b = jj % NB;
-      if (lane == jj && b < nb && row + r < p.n)
-        epilogue(p, b, row + r, acc[r][b], acc[r & ~1][b], acc[(r | 1) % R][b]);
+      for (int jj = 0; jj < R * NB; jj++)
+        if (lane == jj) {
+          v = acc[jj / NB][jj % NB];
+          v_lo = acc[(jj / NB) & ~1][jj % NB];
+          v_hi = acc[((jj / NB) | 1) % R][jj % NB];
+        }
+      const int r = lane / NB, b = lane % NB;
+      if (lane < R * NB && b < nb && row + r < p.n) epilogue(p, b, row + r, v, v_lo, v_hi);
     }
   }
 
@@ -293,9 +306,14 @@ int pick_r(const GemvParams& p) {
   return 4;
 }
 
+// Loads per row in flight per lane: 8 (f32), 4, or 2 for four-row groups (whose block
+// scales ride along in registers).
+template <int WT, int R>
+constexpr int kU = WT == W_F32 ? 8 : R == 4 ? 2 : 4;
+
 template <int WT, int NB, int R>
 void launch_r(const GemvParams& p, cudaStream_t s) {
-  constexpr int U = WT == W_F32 ? 8 : 4;
+  constexpr int U = kU<WT, R>;
   const int groups = (p.n + R - 1) / R;
   int grid = (groups + kWarps - 1) / kWarps;
   if (grid > kGrid) grid = kGrid;
@@ -335,11 +353,10 @@ void launch_t(const GemvParams& p, cudaStream_t s) {
 
 template <int WT, int NB>
 void set_attrs_nb() {
-  constexpr int U = WT == W_F32 ? 8 : 4;
-  cudaFuncSetAttribute(gemv_kernel<WT, NB, 1, U>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-  cudaFuncSetAttribute(gemv_kernel<WT, NB, 2, U>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  cudaFuncSetAttribute(gemv_kernel<WT, NB, 1, kU<WT, 1>>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  cudaFuncSetAttribute(gemv_kernel<WT, NB, 2, kU<WT, 2>>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
   if constexpr (kAllowR4<WT, NB>)
-    cudaFuncSetAttribute(gemv_kernel<WT, NB, 4, U>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    cudaFuncSetAttribute(gemv_kernel<WT, NB, 4, kU<WT, 4>>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
 }
 
 template <int WT>
