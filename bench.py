@@ -47,6 +47,19 @@ CONFIGS = {
 }
 
 
+def profiled_traffic(config: str, family: str):
+    """DRAM bytes (read + write) per launch of the dominant kernel from the ncu capture
+    summarised in profiles/ (`traffic: <config> <family prefix> <bytes>` lines), or None."""
+    f = ROOT / "profiles" / "traffic.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        parts = line.split()
+        if len(parts) == 4 and parts[0] == "traffic:" and parts[1] == config and family.startswith(parts[2]):
+            return int(parts[3])
+    return None
+
+
 def load_peaks() -> tuple[dict, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -250,10 +263,7 @@ def run_ours(args, spec, rank, world, local_rank):
     st.close()
     launches = nk.value
     n_launch_dom = (cfg.num_layers * 4 + 1) if dom.startswith("gemv") else cfg.num_layers
-    traffic = None
-    tfile = ROOT / "profiles" / f"traffic_config{args.config}.json"
-    if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+    traffic = profiled_traffic(args.config, dom)
     hbm = peaks["hbm_gbs"]
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(kern[dom]["gbs"], 1),
                 "peak": hbm, "unit": "GB/s", "frac": round(kern[dom]["gbs"] / hbm, 4),
