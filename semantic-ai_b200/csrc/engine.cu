@@ -483,7 +483,6 @@ State* create_state(Model* m, int max_batch, int max_positions) {
       s->temb_in.alloc(256 * 4);
       s->temb_h.alloc(dim * 4);
       s->temb_o.alloc(dim * 4);
-      s->tsum.alloc(dim * 4);
     }
     // tok_out holds each stream's last argmax (the text token a resumed stream feeds back).
     if (m->kind == 0) check_cuda(cudaMemsetAsync(s->tok_out.p, 0, max_batch * 4, m->stream), "memset");
@@ -939,7 +938,43 @@ void linear_fwd(Model& m, State& s, const Linear& L, const float* x, int64_t x_s
 
 // FlowHead::forward (tts/flow_lm.rs:259-287) and decode (:290-315) from s.z into the latent
 // s.latent_out (which enters holding the noise).
-void enqueue_flow(Model& m, State& s, int nb, int steps, cudaStream_t st) {
+// The flow head's conditioning time input for each decode step i of `steps`: the sum over the
+// TimestepEmbedders of their outputs at t = (i + e) / steps (flow_lm.rs:266-275). It is the same
+// for every stream and frame, so it is computed once per step count, on st, outside any graph
+// capture; null for a head without time embedders.
+const float* time_table(Model& m, State& s, int steps, cudaStream_t st) {
+  const int n_time = (int)m.time_emb.size();
+  if (n_time == 0) return nullptr;
+  auto it = s.time_tables.find(steps);
+  if (it != s.time_tables.end()) return it->second.as<float>();
+  const int dim = m.tts.flow_dim;
+  DevBuf tab;
+  tab.alloc((int64_t)steps * dim * 4);
+  for (int i = 0; i < steps; i++) {
+    for (int e = 0; e < n_time; e++) {
+      const TimeEmbed& te = m.time_emb[e];
+      const float tv = (float)(i + e) / (float)steps;
+      launch_time_input(te.freqs.as<float>(), tv, s.temb_in.as<float>(), st);
+      GemvParams g = gemv_base(te.l1, s.temb_in.as<float>(), 256, 1);
+      g.epi = EPI_SILU;
+      g.out = s.temb_h.as<float>();
+      g.out_stride = dim;
+      launch_gemv(g, st);
+      g = gemv_base(te.l2, s.temb_h.as<float>(), dim, 1);
+      g.epi = EPI_STORE;
+      g.out = s.temb_o.as<float>();
+      g.out_stride = dim;
+      launch_gemv(g, st);
+      launch_time_norm(s.temb_o.as<float>(), dim, te.alpha.as<float>(), tab.as<float>() + (int64_t)i * dim,
+                       e == 0, st);
+    }
+  }
+  check_cuda(cudaGetLastError(), "time table");
+  check_cuda(cudaStreamSynchronize(st), "time table");  // complete before any other stream reads it
+  return s.time_tables.emplace(steps, std::move(tab)).first->second.as<float>();
+}
+
+void enqueue_flow(Model& m, State& s, int nb, int steps, const float* ttab, cudaStream_t st) {
   const auto& t = m.tts;
   const int dim = t.flow_dim, lat = t.latent_dim, d = m.cfg.d_model;
   const int n_time = (int)m.time_emb.size();
@@ -955,26 +990,9 @@ void enqueue_flow(Model& m, State& s, int nb, int steps, cudaStream_t st) {
   linear_fwd(m, s, m.cond_embed, s.z.as<float>(), d, nb, EPI_STORE, y, dim, st);
   const int iters = n_time > 0 ? steps : 1;
   for (int i = 0; i < iters; i++) {
-    if (n_time > 0) {
-      // TimestepEmbedder per time (lsd: i/steps and (i+1)/steps; flow matching: i/steps).
-      for (int e = 0; e < n_time; e++) {
-        const TimeEmbed& te = m.time_emb[e];
-        const float tv = (float)(i + e) / (float)steps;
-        launch_time_input(te.freqs.as<float>(), tv, s.temb_in.as<float>(), st);
-        GemvParams g = gemv_base(te.l1, s.temb_in.as<float>(), 256, 1);
-        g.epi = EPI_SILU;
-        g.out = s.temb_h.as<float>();
-        g.out_stride = dim;
-        launch_gemv(g, st);
-        g = gemv_base(te.l2, s.temb_h.as<float>(), dim, 1);
-        g.epi = EPI_STORE;
-        g.out = s.temb_o.as<float>();
-        g.out_stride = dim;
-        launch_gemv(g, st);
-        launch_time_norm(s.temb_o.as<float>(), dim, te.alpha.as<float>(), s.tsum.as<float>(), e == 0, st);
-      }
-    }
-    launch_cond_silu(y, n_time > 0 ? s.tsum.as<float>() : nullptr,
+    // TimestepEmbedder per time (lsd: i/steps and (i+1)/steps; flow matching: i/steps),
+    // summed: row i of the step count's time table.
+    launch_cond_silu(y, n_time > 0 ? ttab + (int64_t)i * dim : nullptr,
                      n_time > 0 ? (float)(1.0 / (double)n_time) : 0.f, dim, nb, sy, st);
     linear_fwd(m, s, m.input_proj, x, lat, nb, EPI_STORE, xs, dim, st);
     for (const ResBlock& r : m.res) {
@@ -993,7 +1011,7 @@ void enqueue_flow(Model& m, State& s, int nb, int steps, cudaStream_t st) {
 }
 
 // FlowLm::step (tts/flow_lm.rs:162-185) for streams [0, nb).
-void enqueue_tts_step(Model& m, State& s, int nb, int steps, cudaStream_t st) {
+void enqueue_tts_step(Model& m, State& s, int nb, int steps, const float* ttab, cudaStream_t st) {
   const int d = m.cfg.d_model, lat = m.tts.latent_dim;
   linear_fwd(m, s, m.input_linear, s.latent_in.as<float>(), lat, nb, EPI_STORE, s.x.as<float>(), d, st);
   enqueue_layers(m, s, 0, nb, st);
@@ -1003,13 +1021,14 @@ void enqueue_tts_step(Model& m, State& s, int nb, int steps, cudaStream_t st) {
                   s.eos.as<float>(), st);
   check_cuda(cudaMemcpyAsync(s.latent_out.p, s.noise.p, (size_t)nb * lat * 4,
                              cudaMemcpyDeviceToDevice, st), "noise");
-  enqueue_flow(m, s, nb, steps, st);
+  enqueue_flow(m, s, nb, steps, ttab, st);
 }
 
 }  // namespace
 
 int capture_tts_graph(Model& m, State& s, int nb, int steps, cudaStream_t st) {
-  return capture_graph(s, nb + (steps << 16), st, [&] { enqueue_tts_step(m, s, nb, steps, st); });
+  const float* ttab = time_table(m, s, steps, st);  // outside the capture
+  return capture_graph(s, nb + (steps << 16), st, [&] { enqueue_tts_step(m, s, nb, steps, ttab, st); });
 }
 
 void launch_tts_graph(Model& m, State& s, int nb, int steps, cudaStream_t st) {
@@ -1042,7 +1061,7 @@ int64_t enqueue_profile(Model& m, State& s, int nb, int which, cudaStream_t st) 
     return bytes;
   }
   if (which == 2) {
-    enqueue_flow(m, s, nb, 1, st);
+    enqueue_flow(m, s, nb, 1, time_table(m, s, 1, st), st);
     int64_t bytes = m.cond_embed.bytes() + m.input_proj.bytes() + m.final_mod.bytes() + m.final_linear.bytes();
     for (const ResBlock& r : m.res) bytes += r.mod.bytes() + r.mlp1.bytes() + r.mlp2.bytes();
     for (const TimeEmbed& e : m.time_emb) bytes += e.l1.bytes() + e.l2.bytes();

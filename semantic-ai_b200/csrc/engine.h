@@ -132,7 +132,10 @@ struct State {
   DevBuf frames_audio, frames_out;  // svl_stt_run_frames
   // TTS work buffers
   DevBuf latent_in, noise, latent_out, eos, z, y, sy, hbuf, h2buf, modbuf, xs2, tmp;
-  DevBuf temb_in, temb_h, temb_o, tsum, prompt_tok;
+  DevBuf temb_in, temb_h, temb_o, prompt_tok;
+  // TTS: the flow head's summed timestep embeddings, [decode step][flow_dim] per number of
+  // decode steps (they depend on nothing else, so they are computed once).
+  std::map<int, DevBuf> time_tables;
   std::map<int64_t, GemmOperand> xa_by_k;  // bf16 operand maps over xa, keyed by k * 512 + bn
   HostBuf h_tok_in, h_audio_in, h_tok_out, h_err;
   int splits = 1;
