@@ -519,17 +519,14 @@ void set_norm(GemvParams& p, const Norm& N) {
   p.eps = N.eps;
 }
 
-// L2 prefetch of the next layer's copy of a matrix while this layer runs, when a whole
-// layer fits in a half of L2 beside the one being consumed.
-void set_prefetch(GemvParams& g, const Model& m, int l, const Linear& (*pick)(const Layer&)) {
-  const int L = (int)m.layers.size();
-  if (l + 1 >= L) return;
-  const Layer& cur = m.layers[l];
-  const int64_t layer_bytes = cur.in_proj.bytes() + cur.out_proj.bytes() + cur.ff1.bytes() + cur.ff2.bytes();
-  if (layer_bytes > 64ll * 1024 * 1024) return;
-  const Linear& nx = pick(m.layers[l + 1]);
-  g.pf = nx.w.as<uint8_t>();
-  g.pf_bytes = nx.row_stride * nx.n;
+// L2 prefetch of the matrix the next product in the chain reads, while this one runs (the
+// small-batch products are latency-bound and leave HBM idle), when it takes at most a quarter
+// of L2. Measured on STT-1b q8_0, batch 1: 0.533 ms per step with the next layer's copy of
+// the same matrix as the target, 0.519 ms with the next product's, 0.543 ms without.
+void set_prefetch(GemvParams& g, const Linear* next) {
+  if (!next || next->bytes() > 32ll * 1024 * 1024) return;
+  g.pf = next->w.as<uint8_t>();
+  g.pf_bytes = next->row_stride * next->n;
 }
 
 }  // namespace
@@ -583,7 +580,7 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   g.v_ring = vr;
   g.ring_stream_stride = s.ring_stream_stride;
   g.kv_bf16 = s.kv_elt == 2;
-  set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.in_proj; });
+  set_prefetch(g, &L.out_proj);
   lp.in_proj = g;
   // Sliding-window attention (nn/kernels/attention.rs:81-169).
   AttnParams& a = lp.attn;
@@ -617,7 +614,7 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   g.out = x;
   g.out_stride = d;
   g.ls = L.ls1.as<float>();
-  set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.out_proj; });
+  set_prefetch(g, &L.ff1);
   lp.out_proj = g;
   // norm2 + feed-forward (nn/transformer.rs:438-464).
   g = gemv_base(L.ff1, x, d, nb);
@@ -626,14 +623,14 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   g.out_stride = c.ffn_hidden;
   g.epi = c.ffn_kind == SVL_FFN_GATED_SILU ? EPI_SWIGLU
           : c.ffn_kind == SVL_FFN_PLAIN_GELU_ERF ? EPI_GELU_ERF : EPI_GELU_TANH;
-  set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.ff1; });
+  set_prefetch(g, &L.ff2);
   lp.ff1 = g;
   g = gemv_base(L.ff2, act, c.ffn_hidden, nb);
   g.epi = EPI_RESIDUAL;
   g.out = x;
   g.out_stride = d;
   g.ls = L.ls2.as<float>();
-  set_prefetch(g, m, l, [](const Layer& y) -> const Linear& { return y.ff2; });
+  set_prefetch(g, l + 1 < (int)m.layers.size() ? &m.layers[l + 1].in_proj : nullptr);
   lp.ff2 = g;
   return lp;
 }
