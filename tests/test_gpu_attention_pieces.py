@@ -2,11 +2,11 @@
 and against the small-batch attention path.
 
 A batch state of 40 streams has at least 148 (stream, head) units, so its attention runs the
-many-stream kernel: the keys of each unit are cut into pieces, warps take pieces from an
-atomic ticket, and units of several pieces are merged by the last piece. Each stream is put at
-its own position with random imported caches (positions past the window wrap the ring), so
-units have 1 .. 10 pieces. The same streams in one-stream states run the cluster-split
-kernel. Checked for three consecutive steps (the work counters must return to zero after
+many-stream kernel: the keys of each unit are cut into pieces, warps take pieces in a fixed
+round-robin order, and a follow-up kernel merges the partials of units of several pieces. Each
+stream is put at its own position with random imported caches (positions past the window wrap
+the ring), so units have 1 .. 10 pieces. The same streams in one-stream states run the
+cluster-split kernel. Checked for three consecutive steps (the partial buffers are reused by
 every launch):
 - f32 caches: logits within 2e-3 max-abs of the float64 reference (the reference's step over
   the exported caches);
