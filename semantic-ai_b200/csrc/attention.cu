@@ -25,7 +25,7 @@
 namespace svl {
 namespace {
 
-constexpr int kConsumerWarps = 4;
+constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // warp 4: producer
 constexpr int kSlots = 3;
 constexpr int kTileBytes = 16 * 1024;
