@@ -10,9 +10,9 @@
 // step only writes the newest slot, so each CTA bulk-copies its chunk's keys and values into
 // a shared-memory ring *before* griddepcontrol.wait, overlapping the previous kernel; after
 // the wait it reads q and the newest row. Consumer warps score HD/16 lanes per key (16
-// contiguous dims per lane) with an online softmax per lane group; lane groups and warps
-// merge by max-rescaling, and the CTAs of a cluster merge through distributed shared
-// memory. Every mbarrier wait is bounded (a wait that runs out sets *p.err to 4); every CTA
+// contiguous dims per lane) with an online softmax whose running max is shared by the warp's
+// lane groups (they merge by plain sums); warps merge by max-rescaling, and the CTAs of a
+// cluster merge through distributed shared memory. Every mbarrier wait is bounded (a wait that runs out sets *p.err to 4); every CTA
 // reaches both cluster barriers whatever happened, so no CTA waits on one that left.
 #include <cuda.h>
 
@@ -72,17 +72,6 @@ __device__ __forceinline__ void unpack16_global(const uint8_t* src, float* out) 
       out[4 * i + 3] = v.w;
     }
   }
-}
-
-// Merge (m2, l2, a2) into (m, l, a): the max-rescaled sum of two softmax partials.
-__device__ __forceinline__ void merge(float& m, float& l, float* a, float m2, float l2, const float* a2) {
-  const float mn = fmaxf(m, m2);
-  if (mn == -INFINITY) return;
-  const float c1 = exp_ref(m - mn), c2 = exp_ref(m2 - mn);
-  l = l * c1 + l2 * c2;
-#pragma unroll
-  for (int i = 0; i < 16; i++) a[i] = a[i] * c1 + a2[i] * c2;
-  m = mn;
 }
 
 template <int HD, bool BF16>
@@ -220,28 +209,36 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const AttnParams p) {
         for (int t = 0; t < 16; t++) d = fmaf(q[t], kv[t], d);
 #pragma unroll
         for (int o = LPK / 2; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        if (valid) {
-          const float s = p.scale * d;  // scale * dot(q, k), as the reference
-          const float mn = fmaxf(m, s);
-          const float c = exp_ref(m - mn), ev = exp_ref(s - mn);
-          l = l * c + ev;
+        // One running max per warp: the pass's KPW scores raise it (a warp-uniform branch, so
+        // the accumulators are rescaled only when it rises), then each lane group adds its key.
+        const float s = valid ? p.scale * d : -INFINITY;  // scale * dot(q, k), as the reference
+        float mx = s;
 #pragma unroll
-          for (int t = 0; t < 16; t++) acc[t] = acc[t] * c + ev * vv[t];
-          m = mn;
+        for (int o = LPK; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (mx > m) {
+          const float c = exp_ref(m - mx);  // 0 while nothing was added
+          l = l * c;
+#pragma unroll
+          for (int t = 0; t < 16; t++) acc[t] = acc[t] * c;
+          m = mx;
+        }
+        if (valid) {
+          const float ev = exp_ref(s - m);
+          l = l + ev;
+#pragma unroll
+          for (int t = 0; t < 16; t++) acc[t] = acc[t] + ev * vv[t];
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    // Merge the KPW key groups of the warp (lanes sub, sub + LPK, ...).
+    // The KPW key groups of the warp (lanes sub, sub + LPK, ...) share the running max: their
+    // sums add up.
 #pragma unroll
     for (int o = LPK; o < 32; o <<= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-      const float l2 = __shfl_xor_sync(0xffffffffu, l, o);
-      float a2[16];
+      l += __shfl_xor_sync(0xffffffffu, l, o);
 #pragma unroll
-      for (int t = 0; t < 16; t++) a2[t] = __shfl_xor_sync(0xffffffffu, acc[t], o);
-      merge(m, l, acc, m2, l2, a2);
+      for (int t = 0; t < 16; t++) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
     }
     if (kk == 0) {
 #pragma unroll
