@@ -8,8 +8,13 @@ greedy argmax, fed back on the device. Streams are independent, so N GPUs run N 
 batches ("weak" scaling, no collective on the data path).
 
   python bench.py [--config 2] [--gpus N --steps K --warmup W] [--impl ours|reference]
+                  [--layers L] [--no-config3] [--no-cpu-baseline]
 
-The default workload is BASELINE config 2 (STT-1b, q8_0 weights, batch 1, 1000 frames).
+The default workload is BASELINE config 2 (STT-1b, q8_0 weights, batch 1), timed at a steady
+state (every frame attends to the full 750-key window); the same run then measures BASELINE
+config 3 (STT-1b bf16, 256 streams per GPU at staggered fills) under the key "config3".
+--layers L builds the workload with its first L layers only: the small cases for ncu
+captures (such a line is a profiling case, not a benchmark number).
 """
 from __future__ import annotations
 
@@ -33,13 +38,13 @@ from svl import synth  # noqa: E402
 
 CONFIGS = {
     "1": dict(workload="stt-1b f32 batch 1 (BASELINE config 1)", preset="stt_1b", wdt="f32",
-              kv="f32", batch=1, frames=1000),
+              kv="f32", batch=1, frames=1000, steady=True),
     "2": dict(workload="stt-1b q8_0 batch 1 (BASELINE config 2)", preset="stt_1b", wdt="q8_0",
-              kv="f32", batch=1, frames=1000),
+              kv="f32", batch=1, frames=1000, steady=True),
     "3": dict(workload="stt-1b bf16 256 streams/GPU, staggered fills (BASELINE config 3)",
               preset="stt_1b", wdt="bf16", kv="bf16", batch=256, frames=1000, stagger=750),
     "4": dict(workload="stt-2.6b q4_1 batch 1 (BASELINE config 4)", preset="stt_2b6",
-              wdt="q4_1", kv="bf16", batch=1, frames=1500),
+              wdt="q4_1", kv="bf16", batch=1, frames=1500, steady=True),
     "4b": dict(workload="stt-2.6b q4_1 128 streams/GPU (BASELINE config 4)", preset="stt_2b6",
                wdt="q4_1", kv="bf16", batch=128, frames=1500, stagger=375),
     "5": dict(workload="pocket-tts bf16 512 streams/GPU, 64-token prompts (BASELINE config 5)",
@@ -123,32 +128,60 @@ def preset(name: str) -> C.SttConfig:
     return getattr(C, name)()
 
 
-def run_ours(args, spec, rank, world, local_rank):
+def matmul_params(stt, cfg) -> int:
+    """Weights of the step's matrix products (layers + text head): FLOPs per stream-frame = 2x."""
+    d, qd, kvd, F = cfg.d_model, cfg.num_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim, cfg.ffn_hidden
+    per_layer = (qd + 2 * kvd) * d + d * qd + 2 * F * d + d * F
+    return cfg.num_layers * per_layer + stt.text_card * d
+
+
+def init_dist(world, local_rank):
+    if world <= 1:
+        return None
+    import datetime
+    import torch
+    import torch.distributed as dist
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local_rank))
+    return dist
+
+
+def stt_spec_config(spec, layers):
+    import dataclasses
+    stt = preset(spec["preset"])
+    if layers:
+        stt = dataclasses.replace(stt, num_layers=layers)
+    return stt, stt.transformer(spec["wdt"], spec["kv"])
+
+
+def measure_stt(args, spec, rank, world, local_rank, dist, weights=None, full=True):
+    """One STT workload: device-timed stream-frames/s (K frames after W warm-up frames), the
+    same end to end through the host-buffer C-ABI call, the kernel families' rooflines."""
     import torch
     from svl import LanguageModel
     from svl import _lib
 
-    torch.cuda.set_device(local_rank)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
-
-    stt = preset(spec["preset"])
-    cfg = stt.transformer(spec["wdt"], spec["kv"])
+    stt, cfg = stt_spec_config(spec, args.layers)
     B, K, W = spec["batch"], args.steps, args.warmup
-    weights = synth.stt_weights(stt, cfg, seed=0)
+    if weights is None:
+        weights = synth.stt_weights(stt, cfg, seed=0)
     model = LanguageModel(stt, cfg, weights, device=local_rank)
     L = _lib.lib()
     wbytes = model.weight_bytes
+    dev = f"cuda:{local_rank}"
 
     # Per-stream audio: global stream g draws from seed 1 + g; frame 0 sees the initial tokens.
     g0 = rank * B
     audio = synth.audio_tokens(stt, K + W, seed=1 + g0, streams=B)
     rng = np.random.default_rng(2 + rank)
-    offsets = (rng.integers(0, spec["stagger"], size=B) if spec.get("stagger") else np.zeros(B, int))
+    if spec.get("stagger"):
+        offsets = rng.integers(0, spec["stagger"], size=B)
+    elif spec.get("steady") and cfg.context:
+        # Steady state: every timed frame attends to the full window (the stream has run for
+        # at least `window` frames).
+        offsets = np.full(B, cfg.context, int)
+    else:
+        offsets = np.zeros(B, int)
 
     stream = torch.cuda.Stream()
     sptr = ctypes.c_void_p(stream.cuda_stream)
@@ -162,15 +195,15 @@ def run_ours(args, spec, rank, world, local_rank):
                 _lib.check(L.svl_state_import(st.handle, b, 0, None, None, 0, int(offsets[b])))
         return st
 
-    def dev(a):
-        return torch.from_numpy(np.ascontiguousarray(a).view(np.int32)).to(f"cuda:{local_rank}")
+    def to_dev(a):
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int32)).to(dev)
 
-    a_dev = dev(audio)  # [frames][B][n_q]
+    a_dev = to_dev(audio)  # [frames][B][n_q]
     for b in range(B):
         if offsets[b] == 0:
             a_dev[0, b] = stt.card
-    text = [torch.full((B,), stt.text_card, dtype=torch.int32, device=f"cuda:{local_rank}"),
-            torch.zeros(B, dtype=torch.int32, device=f"cuda:{local_rank}")]
+    text = [torch.full((B,), stt.text_card, dtype=torch.int32, device=dev),
+            torch.zeros(B, dtype=torch.int32, device=dev)]
     row = B * stt.n_q * 4
 
     def device_steps(st, first, n):
@@ -206,12 +239,16 @@ def run_ours(args, spec, rank, world, local_rank):
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local_rank}")
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     value = world * B * K / (ms_max / 1000.0)
     st.close()
+
+    out = {"value": round(value, 2), "ms_per_step": round(ms_max / K, 4), "clocks": clk}
+    if not full:
+        return out, model, weights
 
     # End to end through the host-buffer C-ABI call: H2D of the step's tokens and D2H of the
     # argmax inside the timed region, every step.
@@ -227,21 +264,21 @@ def run_ours(args, spec, rank, world, local_rank):
     for i in range(K):
         prev = model.step(prev, aud[i], st)
     e2e_s = time.perf_counter() - t0
-    t = torch.tensor([e2e_s], dtype=torch.float64, device=f"cuda:{local_rank}")
+    t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = world * B * K / float(t.item())
     st.close()
 
-    # Roofline of the dominant kernel family, timed on its launching stream.
+    # Kernel families, timed on their launching stream with every stream at its mean fill of
+    # the timed frames.
     peaks, peak_kind = load_peaks()
     kern = {}
     st = fresh_state()
-    # Put every stream at its steady-state fill for the attention timing.
+    fills = [int(min(o + K // 2, cfg.context or o + K)) for o in offsets]
     for b in range(B):
-        _lib.check(L.svl_state_import(st.handle, b, 0, None, None, 0,
-                                      int(min(offsets[b] + K, cfg.context or offsets[b] + K))))
-    for which, name in ((0, "gemv (all weight products of a step)"), (1, "attention (all layers)")):
+        _lib.check(L.svl_state_import(st.handle, b, 0, None, None, 0, fills[b]))
+    for which, name in ((0, "products (all weight products of a step)"), (1, "attention (all layers)")):
         nbytes = ctypes.c_int64()
         iters = 20
         with torch.cuda.stream(stream):
@@ -253,47 +290,89 @@ def run_ours(args, spec, rank, world, local_rank):
             a1.record(stream)
         stream.synchronize()
         per = a0.elapsed_time(a1) / iters
-        kern[name] = {"ms_per_step": per, "bytes_per_step": nbytes.value,
-                      "gbs": nbytes.value / (per / 1e3) / 1e9}
+        kern[name] = {"ms_per_step": round(per, 5), "bytes_per_step": nbytes.value,
+                      "gbs": round(nbytes.value / (per / 1e3) / 1e9, 1)}
     st.close()
+    prod = kern["products (all weight products of a step)"]
+    flops = 2.0 * matmul_params(stt, cfg) * B
+    prod["tflops"] = round(flops / (prod["ms_per_step"] / 1e3) / 1e12, 2)
     dom = max(kern, key=lambda k: kern[k]["ms_per_step"])
     nk = ctypes.c_int32()
     st = fresh_state()
     _lib.check(L.svl_step_kernel_count(model.handle, st.handle, B, ctypes.byref(nk)))
     st.close()
-    launches = nk.value
-    n_launch_dom = (cfg.num_layers * 4 + 1) if dom.startswith("gemv") else cfg.num_layers
-    traffic = profiled_traffic(args.config, dom)
+    n_launch_dom = (cfg.num_layers * 4 + 1) if dom.startswith("products") else cfg.num_layers
     hbm = peaks["hbm_gbs"]
-    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(kern[dom]["gbs"], 1),
+    src = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["gbs"],
                 "peak": hbm, "unit": "GB/s", "frac": round(kern[dom]["gbs"] / hbm, 4),
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-                "traffic": traffic,
+                "peak_source": src, "traffic": profiled_traffic(spec["key"], dom) if not args.layers else None,
                 "launches_per_step": n_launch_dom,
                 "algorithmic_bytes_per_launch": kern[dom]["bytes_per_step"] // n_launch_dom}
+    if B >= 16:
+        tpk = peaks.get("bf16_tflops_sustained", 1400.0)
+        roofline["tensor"] = {"kernel": "products (tcgen05 GEMMs with their operand preparation)",
+                              "achieved": prod["tflops"], "peak": tpk, "unit": "TFLOP/s",
+                              "frac": round(prod["tflops"] / tpk, 4),
+                              "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained"}
     # Step-level roofline: weights + KV read + KV written per step over HBM bandwidth.
-    kv = sum(C.kv_bytes_per_stream(cfg, int(min(o + K / 2, cfg.context or o + K))) for o in offsets) / 2
-    step_bytes = wbytes + kv + B * cfg.num_layers * 2 * cfg.num_kv_heads * cfg.head_dim * (2 if cfg.kv_dtype == "bf16" else 4)
+    el = 2 if cfg.kv_dtype == "bf16" else 4
+    kv = sum(C.kv_bytes_per_stream(cfg, f) for f in fills)
+    step_bytes = wbytes + kv + B * cfg.num_layers * 2 * cfg.num_kv_heads * cfg.head_dim * el
     step_frac = step_bytes / (ms_max / K / 1e3) / (hbm * 1e9)
-
-    out = {
-        "metric": "stream-frames/s", "value": round(value, 2), "unit": "stream-frames/s",
-        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_max / K, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": spec["wdt"], "data": "synthetic (random-init N(0,0.02) weights seed 0, uniform audio tokens seed 1+stream)",
-        "config": {"workload": spec["workload"], "streams_per_gpu": B, "frames": K,
-                   "d_model": cfg.d_model, "layers": cfg.num_layers, "window": cfg.context,
-                   "kv_dtype": cfg.kv_dtype, "parallelism": f"{world} GPU(s) x {B} independent streams, no collective",
-                   "l2": f"inputs larger than L2: {wbytes / 1e9:.3f} GB of weights streamed per step"},
+    out.update({
         "e2e": {"value": round(e2e_value, 2), "unit": "stream-frames/s",
                 "h2d_bytes_per_step": B * (1 + stt.n_q) * 4, "d2h_bytes_per_step": B * 4},
-        "gpu_launches": launches * K,
+        "gpu_launches": nk.value * K,
         "roofline": roofline,
         "step_roofline": {"bytes_per_step": int(step_bytes), "frac": round(step_frac, 4),
                           "unit": "of measured HBM GB/s"},
         "kernels": kern,
-        "clocks": clk,
+        "config": {"workload": spec["workload"] + (f", first {args.layers} layers only (profiling case)" if args.layers else ""),
+                   "streams_per_gpu": B, "frames": K,
+                   "d_model": cfg.d_model, "layers": cfg.num_layers, "window": cfg.context,
+                   "kv_dtype": cfg.kv_dtype,
+                   "positions": ("steady state: every timed frame attends to the full window"
+                                 if spec.get("steady") else
+                                 f"staggered fills: stream start offsets U[0, {spec['stagger']}) seed 2+rank"
+                                 if spec.get("stagger") else "from position 0"),
+                   "parallelism": f"{world} GPU(s) x {B} independent streams, no collective",
+                   "l2": f"inputs larger than L2: {wbytes / 1e9:.3f} GB of weights + "
+                         f"{kv / 1e9:.3f} GB of KV read per step"},
+    })
+    return out, model, weights
+
+
+def run_ours(args, spec, rank, world, local_rank):
+    import gc
+    import torch
+    torch.cuda.set_device(local_rank)
+    dist = init_dist(world, local_rank)
+    res, model, weights = measure_stt(args, spec, rank, world, local_rank, dist)
+    stt, cfg = stt_spec_config(spec, args.layers)
+    out = {
+        "metric": "stream-frames/s", "value": res["value"], "unit": "stream-frames/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": spec["wdt"], "data": "synthetic (random-init N(0,0.02) weights seed 0, uniform audio tokens seed 1+stream)",
+        "config": res["config"], "e2e": res["e2e"], "gpu_launches": res["gpu_launches"],
+        "roofline": res["roofline"], "step_roofline": res["step_roofline"],
+        "kernels": res["kernels"], "clocks": res["clocks"],
     }
+    del model
+    gc.collect()
+    # BASELINE config 3 in the same run (the north star's many-stream and scaling target):
+    # STT-1b bf16, 256 streams per GPU, from the same seed-0 f32 weights.
+    if args.config == "2" and not args.no_config3 and not args.layers:
+        s3 = dict(CONFIGS["3"], key="3")
+        r3, m3, _ = measure_stt(args, s3, rank, world, local_rank, dist, weights=weights)
+        out["config3"] = {"metric": "stream-frames/s", "value": r3["value"], "unit": "stream-frames/s",
+                          "ms_per_step": r3["ms_per_step"], "dtype": "bf16", "config": r3["config"],
+                          "e2e": r3["e2e"], "gpu_launches": r3["gpu_launches"],
+                          "roofline": r3["roofline"], "step_roofline": r3["step_roofline"],
+                          "kernels": r3["kernels"], "clocks": r3["clocks"]}
+        del m3
+        gc.collect()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(spec, stt, cfg, weights, budget_s=args.cpu_seconds)
     if dist:
@@ -318,12 +397,7 @@ def run_tts(args, spec, rank, world, local_rank):
     from svl import _lib
 
     torch.cuda.set_device(local_rank)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
+    dist = init_dist(world, local_rank)
     cfg, tts = tts_config(spec)
     B, K, W, P = spec["batch"], args.steps, args.warmup, spec["prompt"]
     weights = synth.tts_weights(cfg, tts, seed=0)
@@ -539,35 +613,46 @@ def run_reference(args, spec, rank):
     O.set_threads(threads)
     om = O.OracleModel(0, cfg, weights, stt=stt)
     del weights
-    audio = synth.audio_tokens(stt, args.steps + args.warmup + 1, seed=1)
-    st = om.init_state()
-    prev = stt.text_card
+    # The streams our arm runs at this N: n_gpus x streams per GPU, independent. The sample
+    # steps up to 8 of them round-robin (each with its own state and audio, seed 1 + stream),
+    # one frame each per step: the CPU reads every weight once per stream-frame whatever the
+    # stream count, so the sample's stream-frames/s stands for all of them.
+    total = args.gpus * spec["batch"]
+    ns = min(total, 8)
+    audio = [synth.audio_tokens(stt, args.steps + args.warmup + 1, seed=1 + s) for s in range(ns)]
+    states = [om.init_state() for _ in range(ns)]
+    prev = [stt.text_card] * ns
+
+    def frame(s, i):
+        a = np.full(stt.n_q, stt.card, np.uint32) if i == 0 else audio[s][i]
+        prev[s], _, _ = om.stt_step(prev[s], a, states[s])
+
     for i in range(args.warmup):
-        a = np.full(stt.n_q, stt.card, np.uint32) if i == 0 else audio[i]
-        prev, _, _ = om.stt_step(prev, a, st)
-    # Each step: one stream-frame (the whole step at batch 1; a one-stream sample otherwise),
-    # stopping early once the time budget is spent.
+        for s in range(ns):
+            frame(s, i)
+    # Each step: one frame of each sampled stream, stopping early once the time budget is spent.
     n = 0
     t0 = time.perf_counter()
     for i in range(args.steps):
         if time.perf_counter() - t0 > args.ref_seconds:
             break
-        a = audio[args.warmup + i] if args.warmup + i > 0 else np.full(stt.n_q, stt.card, np.uint32)
-        prev, _, _ = om.stt_step(prev, a, st)
+        for s in range(ns):
+            frame(s, args.warmup + i)
         n += 1
     dt = time.perf_counter() - t0
-    value = n / dt
+    value = n * ns / dt
+    sample = (f"{n} frames of each of {ns} streams (of the {total} the GPU arm runs at this N) after "
+              f"{args.warmup} warm-up frames, {dt:.1f} s on {threads} threads (C restatement of the "
+              f"reference CPU path; the Rust reference needs cargo and candle 0.11.1, absent here)")
     out = {"metric": "stream-frames/s", "value": round(value, 3), "unit": "stream-frames/s",
            "n_gpus": args.gpus, "steps": n, "warmup": args.warmup,
            "ms_per_step": round(dt / max(n, 1) * 1e3, 3), "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": spec["wdt"], "data": "synthetic",
-           "config": {"workload": spec["workload"], "streams_per_gpu": spec["batch"]},
+           "config": {"workload": spec["workload"], "streams_per_gpu": spec["batch"],
+                      "streams_sampled": ns},
            "impl": "reference",
            "cpu_baseline": {"value": round(value, 3), "unit": "stream-frames/s", "cores": threads,
-                            "kind": "port",
-                            "sample": f"{n} frames of one stream after {args.warmup} warm-up frames "
-                                      f"(C restatement of the reference CPU path; the Rust reference "
-                                      f"needs cargo and candle 0.11.1, absent here)"},
+                            "kind": "port", "sample": sample},
            "e2e": {"value": round(value, 3), "unit": "stream-frames/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
@@ -583,8 +668,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-seconds", type=float, default=120.0)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="first L layers only: a small case for profiling captures")
+    ap.add_argument("--no-config3", action="store_true",
+                    help="skip the config-3 block of the default (config 2) run")
     args = ap.parse_args()
-    spec = CONFIGS[args.config]
+    spec = dict(CONFIGS[args.config], key=args.config)
     if args.steps is None:
         args.steps = spec["frames"]
     args.warmup = max(args.warmup, 3)

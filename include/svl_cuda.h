@@ -115,6 +115,20 @@ SVL_API int64_t svl_model_weight_bytes(const svl_model* model);
  * without a window) and its own position. */
 SVL_API svl_status svl_state_create(svl_model* model, int32_t max_batch, int32_t max_positions,
                                     svl_state** out);
+/* svl_state_create with options; flags is a combination of:
+ *   SVL_STATE_REFERENCE_ORDER: every reduction whose order the reference's CPU path fixes
+ *     runs in that order -- the norm sums element by element (candle rms_norm / layer_norm),
+ *     the attention key by key (nn/kernels/attention.rs:142-169), RoPE from a table of the C
+ *     library's cosf / sinf evaluated at state creation (nn/transformer.rs:159-166) -- and
+ *     the f32 / bf16 weight products in kernels::dot's lane order (nn/kernels/mod.rs:68-91),
+ *     so that a step reproduces the reference CPU arithmetic bit for bit on identical
+ *     inputs. Quantised products use the reference order in every state. Slower (norm and
+ *     softmax sums become serial chains; many-stream products stay off the tensor cores);
+ *     positions are limited to max(max_positions, 8192) and rings to 51,200 keys.
+ * No counterpart in the reference (whose CPU path is this order). */
+#define SVL_STATE_REFERENCE_ORDER 1u
+SVL_API svl_status svl_state_create_ex(svl_model* model, int32_t max_batch, int32_t max_positions,
+                                       uint32_t flags, svl_state** out);
 SVL_API void svl_state_destroy(svl_state* state);
 /* Back to position 0 (a fresh init_state) for one stream, or all when stream < 0. */
 SVL_API svl_status svl_state_reset(svl_state* state, int32_t stream);

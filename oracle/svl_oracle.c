@@ -328,18 +328,31 @@ static float vec_dot_q8_0_avx2(const blk_q8_0* w, const blk_q8_0* x, int nb) {
 }
 #endif
 
+/* Q4_1 x Q8_1 block dot in the order of ggml's AVX2 vec_dot_q4_1_q8_1 (Q4_1 has no
+ * counterpart in the reference; this is the published x86 form of the format's dot). The
+ * 32 nibbles unpack to values 0..15 (low nibbles of bytes 0..15) and 16..31 (high nibbles);
+ * lane l sums the four products of values 4l..4l+3 and accumulates d_w*d_x times that sum
+ * with an FMA, block after block; m_w * s_x is summed separately (product rounded, then
+ * added). Result: the hsum tree of the lanes (as in vec_dot_q8_0) plus that sum. */
 static float vec_dot_q4_1(const blk_q4_1* w, const blk_q8_1* x, int nb) {
-  float sumf = 0.0f;
+  float acc[8] = {0};
+  float summs = 0.0f;
   for (int b = 0; b < nb; b++) {
-    int32_t sumi = 0;
-    for (int j = 0; j < QK / 2; j++) {
-      sumi += (int32_t)(w[b].qs[j] & 0x0f) * x[b].qs[j];
-      sumi += (int32_t)(w[b].qs[j] >> 4) * x[b].qs[j + QK / 2];
-    }
+    float mprod = orc_f16_to_f32(w[b].m) * orc_f16_to_f32(x[b].s);
+    summs = summs + mprod;
     float dd = orc_f16_to_f32(w[b].d) * orc_f16_to_f32(x[b].d);
-    sumf += dd * (float)sumi + orc_f16_to_f32(w[b].m) * orc_f16_to_f32(x[b].s);
+    for (int l = 0; l < 8; l++) {
+      int32_t s = 0;
+      for (int e = 0; e < 4; e++) {
+        int v = 4 * l + e;
+        int q = v < QK / 2 ? (w[b].qs[v] & 0x0f) : (w[b].qs[v - QK / 2] >> 4);
+        s += (int32_t)q * (int32_t)x[b].qs[v];
+      }
+      acc[l] = fmaf(dd, (float)s, acc[l]);
+    }
   }
-  return sumf;
+  float r0 = acc[0] + acc[4], r1 = acc[1] + acc[5], r2 = acc[2] + acc[6], r3 = acc[3] + acc[7];
+  return ((r0 + r2) + (r1 + r3)) + summs;
 }
 
 static void matvec_q8_0_blocks(const blk_q8_0* xq, const uint8_t* wblocks, int n, int k,

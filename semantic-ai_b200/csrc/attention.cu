@@ -12,8 +12,10 @@
 // the wait it reads q and the newest row. Consumer warps score HD/16 lanes per key (16
 // contiguous dims per lane) with an online softmax whose running max is shared by the warp's
 // lane groups (they merge by plain sums); warps merge by max-rescaling, and the CTAs of a
-// cluster merge through distributed shared memory. Every mbarrier wait is bounded (a wait that runs out sets *p.err to 4); every CTA
-// reaches both cluster barriers whatever happened, so no CTA waits on one that left.
+// cluster merge through distributed shared memory: each pushes its partial into the first CTA's
+// shared memory, and one cluster barrier publishes them. Every mbarrier wait is bounded (a wait
+// that runs out sets *p.err to 4); every CTA reaches the cluster barrier whatever happened, so
+// no CTA waits on one that left.
 #include <cuda.h>
 
 #include <algorithm>
@@ -26,7 +28,7 @@ namespace svl {
 namespace {
 
 constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;  // warp 4: producer
+constexpr int kThreads = (kConsumerWarps + 1) * 32;  // warp kConsumerWarps: producer
 constexpr int kSlots = 3;
 constexpr int kTileBytes = 16 * 1024;
 constexpr int kMaxSplits = 8;  // portable cluster size
@@ -90,6 +92,10 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const AttnParams p) {
   __shared__ float sm_a[kConsumerWarps][HD];
   __shared__ float part_m, part_l;
   __shared__ float part_a[HD];
+  // The cluster's first CTA collects every chunk's partial here (written by the chunks'
+  // CTAs through distributed shared memory).
+  __shared__ float gm[kMaxSplits], gl[kMaxSplits];
+  __shared__ float ga[kMaxSplits][HD];
   __shared__ int failed;
 
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -142,8 +148,12 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const AttnParams p) {
     }
   };
   int issued = 0;
-  if (warp == kConsumerWarps && lane == 0)
+  if (warp == kConsumerWarps && lane == 0) {
     for (; issued < min(kSlots, ntiles); issued++) issue(issued);
+    // Then this CTA's share of the later kernels' data into L2.
+    const int cta = split + p.splits * (h + p.heads * b), ctas = p.splits * p.heads * p.nb;
+    for (int i = 0; i < kMaxPrefetch; i++) prefetch_l2_share(p.pf[i].p, p.pf[i].bytes, cta, ctas);
+  }
   pdl_launch();
   pdl_wait();
 
@@ -267,6 +277,15 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const AttnParams p) {
       part_m = M;
       part_l = L;
     }
+    if (p.splits > 1) {
+      // Push the partial into the first CTA's collection (stores do not wait on the remote
+      // CTA; the cluster barrier below publishes them).
+      dsmem_st(dsmem_addr(&ga[split][tid], 0), A);
+      if (tid == 0) {
+        dsmem_st(dsmem_addr(&gm[split], 0), M);
+        dsmem_st(dsmem_addr(&gl[split], 0), L);
+      }
+    }
   }
   const int64_t bh = (int64_t)b * p.heads + h;
   if (p.splits == 1) {
@@ -274,23 +293,22 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const AttnParams p) {
     if (tid < HD) p.out[bh * HD + tid] = part_l > 0.f ? part_a[tid] / part_l : 0.f;
     return;
   }
-  // The chunks of this (stream, head) merge in the cluster's first CTA, in chunk order.
+  // The chunks of this (stream, head) merge in the cluster's first CTA, in chunk order. After
+  // the barrier no CTA touches another's shared memory, so the others may leave.
   cluster_sync();
   if (split == 0 && tid < HD) {
     float MM = -INFINITY;
-    for (int s = 0; s < p.splits; s++) MM = fmaxf(MM, dsmem_ld(dsmem_addr(&part_m, s)));
+    for (int s = 0; s < p.splits; s++) MM = fmaxf(MM, gm[s]);
     float LL = 0.f, AA = 0.f;
     for (int s = 0; s < p.splits; s++) {
-      const float ms = dsmem_ld(dsmem_addr(&part_m, s));
+      const float ms = gm[s];
       if (ms == -INFINITY) continue;
       const float c = exp_ref(ms - MM);
-      LL = LL + dsmem_ld(dsmem_addr(&part_l, s)) * c;
-      AA = AA + dsmem_ld(dsmem_addr(&part_a[tid], s)) * c;
+      LL = LL + gl[s] * c;
+      AA = AA + ga[s][tid] * c;
     }
     p.out[bh * HD + tid] = LL > 0.f ? AA / LL : 0.f;
   }
-  // Keep every CTA's shared memory alive until the first CTA has read it.
-  cluster_sync();
 }
 
 // ---- many streams: pieces of a fixed key count -----------------------------------------

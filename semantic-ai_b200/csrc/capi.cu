@@ -38,13 +38,18 @@ void check_stream(svl::State& s, int stream) {
   need(stream >= 0 && stream < s.max_batch, SVL_ERR_INVALID_INPUT, "stream index out of range");
 }
 
-// Positions beyond the ring are an error without a window (the reference's cache grows).
-void check_room(svl::State& s, int nb, int steps) {
-  if (s.windowed) return;
-  for (int b = 0; b < nb; b++)
-    if (s.hpos[b] + steps > s.cap)
+// Positions beyond the ring are an error without a window (the reference's cache grows), and
+// in reference order positions past the state's RoPE table are not supported.
+void check_room(svl::State& s, int b0, int nb, int steps) {
+  for (int b = b0; b < b0 + nb; b++) {
+    if (!s.windowed && s.hpos[b] + steps > s.cap)
       throw Error(SVL_ERR_INVALID_INPUT, "stream would exceed the state's max_positions");
+    if (s.ref_order && s.hpos[b] + steps > s.rope_positions)
+      throw Error(SVL_ERR_UNSUPPORTED, "reference order covers positions below " +
+                                           std::to_string(s.rope_positions) + " (its RoPE table)");
+  }
 }
+void check_room(svl::State& s, int nb, int steps) { check_room(s, 0, nb, steps); }
 
 }  // namespace
 
@@ -96,6 +101,17 @@ SVL_API svl_status svl_state_create(svl_model* model, int32_t max_batch, int32_t
     need(model && out, SVL_ERR_INVALID_INPUT, "null argument");
     *out = nullptr;
     svl::State* s = svl::create_state(model->m, max_batch, max_positions);
+    *out = new svl_state{s, model};
+  });
+}
+
+SVL_API svl_status svl_state_create_ex(svl_model* model, int32_t max_batch, int32_t max_positions,
+                                       uint32_t flags, svl_state** out) {
+  return guarded([&] {
+    need(model && out, SVL_ERR_INVALID_INPUT, "null argument");
+    need((flags & ~SVL_STATE_REFERENCE_ORDER) == 0, SVL_ERR_INVALID_INPUT, "unknown state flags");
+    *out = nullptr;
+    svl::State* s = svl::create_state(model->m, max_batch, max_positions, flags);
     *out = new svl_state{s, model};
   });
 }
@@ -315,8 +331,7 @@ SVL_API svl_status svl_transformer_forward(svl_model* model, svl_state* state, i
     need(s.m == &m, SVL_ERR_INVALID_INPUT, "state of another model");
     check_stream(s, stream);
     need(t >= 1, SVL_ERR_INVALID_INPUT, "t must be positive");
-    if (!s.windowed && s.hpos[stream] + t > s.cap)
-      throw Error(SVL_ERR_INVALID_INPUT, "stream would exceed the state's max_positions");
+    check_room(s, stream, 1, t);
     svl::check_cuda(cudaSetDevice(m.device), "cudaSetDevice");
     cudaStream_t st = m.stream;
     const int d = m.cfg.d_model;
@@ -394,9 +409,7 @@ void tts_prompt(svl::Model& m, svl::State& s, int b0, int nb, const uint32_t* to
   for (int64_t i = 0; i < (int64_t)nb * n; i++)
     if (tokens[i] > (uint32_t)m.tts.text_bins)
       throw Error(SVL_ERR_INVALID_INPUT, "text token " + std::to_string(tokens[i]) + " out of range");
-  for (int b = b0; b < b0 + nb; b++)
-    if (!s.windowed && s.hpos[b] + n > s.cap)
-      throw Error(SVL_ERR_INVALID_INPUT, "stream would exceed the state's max_positions");
+  check_room(s, b0, nb, n);
   svl::check_cuda(cudaSetDevice(m.device), "cudaSetDevice");
   cudaStream_t st = m.stream;
   const size_t bytes = (size_t)nb * n * 4;

@@ -125,6 +125,8 @@ struct Loader {
     L.interleave = interleave;
     L.row_stride = packed_row_stride(wt, k);
     L.w.alloc(L.row_stride * n_out);
+    // Zero first: the unused blocks of a partial last super-block stay zero.
+    check_cuda(cudaMemsetAsync(L.w.p, 0, L.row_stride * n_out, m.stream), "memset");
     float* src = stage(v);
     launch_pack_linear(src, L.w.as<uint8_t>(), L.row_stride, n_out, k, wt, interleave, m.stream);
     check_cuda(cudaStreamSynchronize(m.stream), "pack weights");
@@ -229,8 +231,8 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
   check_cuda(cudaSetDevice(device), "cudaSetDevice");
   gemv_init_device();
   gemm_init_device();
-  step_kernel_init_device();
   attention_init_device();
+  attention_ref_init_device();
   Model* m = new Model();
   try {
     m->kind = kind;
@@ -319,8 +321,6 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
   return m;
 }
 
-void build_step_program(Model& m, State& s);
-
 // Many streams over Q8_0 / Q4_1 weights run on the tensor cores from f16 images of the
 // dequantised matrices, built once per model when the first such state is created (the
 // packed weights stay in use for small batches). The images hold the values the quantised
@@ -363,17 +363,10 @@ void raise_device_error(State& s, cudaStream_t st) {
   throw Error(SVL_ERR_TIMEOUT, "a bounded device-side wait ran out (code " + std::to_string(e) + ")");
 }
 
-// SVL_STEP_KERNEL=1 runs the batch-1 step as the persistent step kernel (stepk.cu), read when
-// a state is created. It is off by default: on B200 it measures 0.76 ms per STT-1b q8_0 step
-// against 0.74 ms for the separate-kernel path. Its producer alone streams the step's bytes
-// in 215 us (78% of HBM); the consumers are latency-bound between the grid-wide phase
-// barriers (82 per step), which is the work left on it.
-bool step_kernel_disabled() {
-  const char* v = std::getenv("SVL_STEP_KERNEL");
-  return !(v && v[0] == '1');
-}
+// Positions a reference-order state's RoPE table covers when max_positions does not say.
+constexpr int kRefRopePositions = 8192;
 
-State* create_state(Model* m, int max_batch, int max_positions) {
+State* create_state(Model* m, int max_batch, int max_positions, uint32_t flags) {
   if (max_batch <= 0) throw Error(SVL_ERR_INVALID_INPUT, "max_batch must be positive");
   check_cuda(cudaSetDevice(m->device), "cudaSetDevice");
   const auto& c = m->cfg;
@@ -384,6 +377,26 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     s->windowed = c.context > 0;
     s->cap = s->windowed ? c.context : max_positions;
     if (s->cap <= 0) throw Error(SVL_ERR_INVALID_INPUT, "max_positions must be positive without a window");
+    s->ref_order = (flags & SVL_STATE_REFERENCE_ORDER) != 0;
+    if (s->ref_order) {
+      if (!attention_ref_supported(c.head_dim, s->cap))
+        throw Error(SVL_ERR_UNSUPPORTED, "reference order: the ring is too long for the in-order attention");
+      // (cos, sin)(pos * inv_freq[i]) with the C library's cosf / sinf, as the reference's
+      // forward_block evaluates its RoPE table (nn/transformer.rs:159-166).
+      const int half = c.head_dim / 2;
+      s->rope_positions = std::max(max_positions, kRefRopePositions);
+      std::vector<float> inv(half), tab((size_t)s->rope_positions * half * 2);
+      check_cuda(cudaMemcpy(inv.data(), m->inv_freq.p, half * 4, cudaMemcpyDeviceToHost), "d2h");
+      for (int pos = 0; pos < s->rope_positions; pos++)
+        for (int i = 0; i < half; i++) {
+          const float f = (float)pos * inv[i];
+          tab[((size_t)pos * half + i) * 2] = cosf(f);
+          tab[((size_t)pos * half + i) * 2 + 1] = sinf(f);
+        }
+      s->rope_tab.alloc(tab.size() * 4);
+      check_cuda(cudaMemcpyAsync(s->rope_tab.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, m->stream), "upload");
+      check_cuda(cudaStreamSynchronize(m->stream), "upload");
+    }
     s->kv_elt = c.kv_dtype == SVL_DT_BF16 ? 2 : 4;
     s->ring_stream_stride = (int64_t)c.num_kv_heads * s->cap * c.head_dim;
     s->ring_layer_stride = s->ring_stream_stride * max_batch;
@@ -425,7 +438,7 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     s->am_val.alloc(cand * 4);
     s->am_idx.alloc(cand * 4);
     const bool quantised = c.weight_dtype == SVL_DT_Q8_0 || c.weight_dtype == SVL_DT_Q4_1;
-    if ((c.weight_dtype == SVL_DT_BF16 || quantised) && max_batch >= kGemmMinBatch) {
+    if ((c.weight_dtype == SVL_DT_BF16 || quantised) && max_batch >= kGemmMinBatch && !s->ref_order) {
       if (quantised) ensure_shadows(*m);
       const int kx = std::max({d, qd, m->kind == 1 ? m->tts.flow_dim : 0, m->kind == 1 ? m->tts.latent_dim : 0});
       s->xa.alloc((int64_t)max_batch * kx * 2);
@@ -486,7 +499,6 @@ State* create_state(Model* m, int max_batch, int max_positions) {
     }
     // tok_out holds each stream's last argmax (the text token a resumed stream feeds back).
     if (m->kind == 0) check_cuda(cudaMemsetAsync(s->tok_out.p, 0, max_batch * 4, m->stream), "memset");
-    if (m->kind == 0 && !step_kernel_disabled()) build_step_program(*m, *s);
     check_cuda(cudaStreamSynchronize(m->stream), "state init");
   } catch (...) {
     delete s;
@@ -512,6 +524,13 @@ GemvParams gemv_base(const Linear& L, const float* x, int64_t x_stride, int nb) 
   return p;
 }
 
+GemvParams gemv_base(const Linear& L, const float* x, int64_t x_stride, int nb, const State& s) {
+  GemvParams p = gemv_base(L, x, x_stride, nb);
+  p.ref_order = s.ref_order;
+  p.err = s.err.as<int>();
+  return p;
+}
+
 void set_norm(GemvParams& p, const Norm& N) {
   p.norm = N.kind;
   p.norm_w = N.w.as<float>();
@@ -519,14 +538,25 @@ void set_norm(GemvParams& p, const Norm& N) {
   p.eps = N.eps;
 }
 
-// L2 prefetch of the matrix the next product in the chain reads, while this one runs (the
-// small-batch products are latency-bound and leave HBM idle), when it takes at most a quarter
-// of L2. Measured on STT-1b q8_0, batch 1: 0.533 ms per step with the next layer's copy of
-// the same matrix as the target, 0.519 ms with the next product's, 0.543 ms without.
-void set_prefetch(GemvParams& g, const Linear* next) {
-  if (!next || next->bytes() > 32ll * 1024 * 1024) return;
-  g.pf = next->w.as<uint8_t>();
-  g.pf_bytes = next->row_stride * next->n;
+// L2 prefetches (the small-batch kernels are latency-bound and leave HBM idle between their
+// dependent steps): every kernel of a layer pulls into L2 the data of the kernel two places
+// after it in the chain -- in_proj: out_proj's matrix; attention: linear_in's; out_proj:
+// linear_out's; linear_in: the next layer's in_proj (or the text head); linear_out: the next
+// layer's K and V rings -- and the head pulls layer 0's in_proj and rings for the next step.
+// A range is prefetched only when it takes at most a quarter of L2.
+constexpr int64_t kPrefetchMax = 32ll * 1024 * 1024;
+
+PrefetchRange weights_range(const Linear* L) {
+  if (!L || L->row_stride * L->n > kPrefetchMax) return PrefetchRange{};
+  return PrefetchRange{L->w.as<uint8_t>(), L->row_stride * L->n};
+}
+
+// Layer l's K (v = 0) or V (v = 1) ring of streams [b0, b0 + nb): one contiguous run.
+PrefetchRange ring_range(const State& s, int l, int b0, int nb, int v) {
+  const int64_t bytes = (int64_t)nb * s.ring_stream_stride * s.kv_elt;
+  if (bytes > kPrefetchMax) return PrefetchRange{};
+  const DevBuf& r = v ? s.v_ring : s.k_ring;
+  return PrefetchRange{r.as<uint8_t>() + ((int64_t)l * s.ring_layer_stride + (int64_t)b0 * s.ring_stream_stride) * s.kv_elt, bytes};
 }
 
 }  // namespace
@@ -564,7 +594,7 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   uint8_t* vr = s.v_ring.as<uint8_t>() + ((int64_t)l * s.ring_layer_stride + (int64_t)b0 * s.ring_stream_stride) * s.kv_elt;
   LayerParams lp;
   // norm1 + in_proj + RoPE + KV-ring write (nn/transformer.rs:329-342).
-  GemvParams g = gemv_base(L.in_proj, x, d, nb);
+  GemvParams g = gemv_base(L.in_proj, x, d, nb, s);
   set_norm(g, L.norm1);
   g.epi = EPI_QKV_ROPE;
   g.out = q;
@@ -580,7 +610,9 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   g.v_ring = vr;
   g.ring_stream_stride = s.ring_stream_stride;
   g.kv_bf16 = s.kv_elt == 2;
-  set_prefetch(g, &L.out_proj);
+  g.rope_by_pos = s.rope_tab.as<float2>();
+  g.rope_positions = s.rope_positions;
+  g.pf[0] = weights_range(&L.out_proj);
   lp.in_proj = g;
   // Sliding-window attention (nn/kernels/attention.rs:81-169).
   AttnParams& a = lp.attn;
@@ -608,29 +640,34 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   a.ring_row0 = b0 * c.num_kv_heads * s.cap;
   a.out = attn;
   a.err = s.err.as<int>();
+  a.pf[0] = weights_range(&L.ff1);
   // out_proj + residual (nn/transformer.rs:344, :239-243).
-  g = gemv_base(L.out_proj, attn, qd, nb);
+  g = gemv_base(L.out_proj, attn, qd, nb, s);
   g.epi = EPI_RESIDUAL;
   g.out = x;
   g.out_stride = d;
   g.ls = L.ls1.as<float>();
-  set_prefetch(g, &L.ff1);
+  g.pf[0] = weights_range(&L.ff2);
   lp.out_proj = g;
   // norm2 + feed-forward (nn/transformer.rs:438-464).
-  g = gemv_base(L.ff1, x, d, nb);
+  g = gemv_base(L.ff1, x, d, nb, s);
   set_norm(g, L.norm2);
   g.out = act;
   g.out_stride = c.ffn_hidden;
   g.epi = c.ffn_kind == SVL_FFN_GATED_SILU ? EPI_SWIGLU
           : c.ffn_kind == SVL_FFN_PLAIN_GELU_ERF ? EPI_GELU_ERF : EPI_GELU_TANH;
-  set_prefetch(g, &L.ff2);
+  const bool last = l + 1 == (int)m.layers.size();
+  g.pf[0] = weights_range(!last ? &m.layers[l + 1].in_proj : m.kind == 0 ? &m.text_linear : nullptr);
   lp.ff1 = g;
-  g = gemv_base(L.ff2, act, c.ffn_hidden, nb);
+  g = gemv_base(L.ff2, act, c.ffn_hidden, nb, s);
   g.epi = EPI_RESIDUAL;
   g.out = x;
   g.out_stride = d;
   g.ls = L.ls2.as<float>();
-  set_prefetch(g, l + 1 < (int)m.layers.size() ? &m.layers[l + 1].in_proj : nullptr);
+  if (!last) {
+    g.pf[0] = ring_range(s, l + 1, b0, nb, 0);
+    g.pf[1] = ring_range(s, l + 1, b0, nb, 1);
+  }
   lp.ff2 = g;
   return lp;
 }
@@ -658,7 +695,12 @@ void enqueue_layers_mask(Model& m, State& s, int b0, int nb, cudaStream_t st, bo
     } else if (do_lin) {
       launch_gemv(g, st);
     }
-    if (do_attn) launch_attention_decode(lp.attn, st);
+    if (do_attn) {
+      if (s.ref_order)
+        launch_attention_ref(lp.attn, st);
+      else
+        launch_attention_decode(lp.attn, st);
+    }
     if (!do_lin) continue;
     g = lp.out_proj;
     if (tc) {
@@ -697,7 +739,7 @@ void launch_extra_heads(const float* logits, int nb, int heads, int dim, float* 
 namespace {
 
 GemvParams head_params(Model& m, State& s, int nb) {
-  GemvParams g = gemv_base(m.text_linear, s.x.as<float>(), m.cfg.d_model, nb);
+  GemvParams g = gemv_base(m.text_linear, s.x.as<float>(), m.cfg.d_model, nb, s);
   set_norm(g, m.out_norm);
   g.epi = EPI_LOGITS;
   g.out = s.logits.as<float>();
@@ -706,90 +748,14 @@ GemvParams head_params(Model& m, State& s, int nb) {
   g.am_idx = s.am_idx.as<int>();
   g.am_ticket = s.am_ticket.as<unsigned>();
   g.tokens = s.tok_out.as<uint32_t>();
+  // The next step starts with layer 0.
+  g.pf[0] = weights_range(&m.layers[0].in_proj);
+  g.pf[1] = ring_range(s, 0, 0, nb, 0);
+  g.pf[2] = ring_range(s, 0, 0, nb, 1);
   return g;
 }
 
 }  // namespace
-
-// Builds the persistent batch-1 step for stream 0 when the model fits its limits: an STT model
-// without extra heads, one weight format, k <= 10240, head_dim a multiple of 32 up to 128, and
-// at most 1024 keys per attention part. Otherwise step_ctas stays 0.
-void build_step_program(Model& m, State& s) {
-  const auto& c = m.cfg;
-  if (m.kind != 0 || m.stt.extra_heads_num > 0 || c.head_dim % 32 || c.head_dim > 128) return;
-  const int wt = m.text_linear.wtype;
-  const int ctas = step_kernel_ctas(wt);
-  if (ctas < c.num_heads) return;
-  std::vector<StepPhase> ph;
-  int64_t slot = 16 * 1024, rec = 0;
-  auto add_gemv = [&](const GemvParams& g) {
-    if (g.wtype != wt || g.k > 10240) return false;
-    const bool pairs = g.epi == EPI_QKV_ROPE || g.epi == EPI_SWIGLU;
-    slot = std::max<int64_t>(slot, (pairs ? 2 : 1) * g.row_stride);
-    rec = std::max<int64_t>(rec, rec_bytes_of(wt, g.k));
-    StepPhase p{};
-    p.type = PH_GEMV;
-    p.g = g;
-    p.g.pf = nullptr;
-    p.g.pf_bytes = 0;
-    ph.push_back(p);
-    return true;
-  };
-  StepPhase e{};
-  e.type = PH_EMBED;
-  e.e.text_table = m.text_emb.p;
-  e.e.audio_tables = m.audio_emb.p;
-  e.e.tables_bf16 = m.tables_bf16;
-  e.e.text_tok = s.tok_in.as<uint32_t>();
-  e.e.audio_tok = s.audio_in.as<uint32_t>();
-  e.e.nb = 1;
-  e.e.d = c.d_model;
-  e.e.n_q = m.stt.n_q;
-  e.e.card = m.stt.card;
-  e.e.text_card = m.stt.text_card;
-  e.e.x = s.x.as<float>();
-  e.e.error_flag = s.err.as<int>();
-  ph.push_back(e);
-  const int splits = std::max(1, ctas / c.num_heads);
-  const int keys = c.context > 0 ? c.context : s.cap;
-  if ((keys + splits - 1) / splits > 1024) return;
-  for (int l = 0; l < c.num_layers; l++) {
-    LayerParams lp = layer_params(m, s, l, 0, 1);
-    if (!add_gemv(lp.in_proj)) return;
-    StepPhase a{};
-    a.type = PH_ATTN;
-    a.a = lp.attn;
-    ph.push_back(a);
-    if (!add_gemv(lp.out_proj) || !add_gemv(lp.ff1) || !add_gemv(lp.ff2)) return;
-  }
-  GemvParams h = head_params(m, s, 1);
-  h.pos_advance = s.pos.as<int>();
-  if (!add_gemv(h)) return;
-  slot = (slot + 15) / 16 * 16;
-  rec = std::max<int64_t>((rec + 15) / 16 * 16, (int64_t)(1 + m.stt.n_q) * 16 * ((c.d_model / 4 + ctas - 1) / ctas));
-  const int nslots = (int)std::min<int64_t>(16, (kStepDynSmem - rec) / slot);
-  if (nslots < 4 || rec > kStepRecBytes) return;
-  s.step_phases.alloc(ph.size() * sizeof(StepPhase));
-  check_cuda(cudaMemcpyAsync(s.step_phases.p, ph.data(), ph.size() * sizeof(StepPhase),
-                             cudaMemcpyHostToDevice, m.stream), "upload");
-  s.step_counter_bytes = (ph.size() + (size_t)c.num_layers * c.num_heads) * 4;
-  s.step_counters.alloc(s.step_counter_bytes);
-  check_cuda(cudaMemsetAsync(s.step_counters.p, 0, s.step_counter_bytes, m.stream), "memset");
-  s.step_part.alloc((size_t)c.num_heads * splits * (c.head_dim + 2) * 4);
-  check_cuda(cudaStreamSynchronize(m.stream), "step program");
-  StepProgram& pg = s.step_pg;
-  pg.ph = s.step_phases.as<StepPhase>();
-  pg.nph = (int)ph.size();
-  pg.done = s.step_counters.as<unsigned>();
-  pg.head_cnt = pg.done + ph.size();
-  pg.part = s.step_part.as<float>();
-  pg.splits = splits;
-  pg.slot_bytes = (int)slot;
-  pg.nslots = nslots;
-  pg.rec_bytes = (int)rec;
-  pg.err = s.err.as<int>();
-  s.step_ctas = ctas;
-}
 
 // The logits product with its argmax: on the tensor cores (out_norm as the operand prep)
 // when the step's products run there.
@@ -807,13 +773,6 @@ void launch_head(Model& m, State& s, const GemvParams& g, cudaStream_t st) {
 
 void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
   const auto& c = m.cfg;
-  if (nb == 1 && s.step_ctas > 0) {
-    // The whole batch-1 step as one persistent kernel (stepk.cu).
-    check_cuda(cudaMemsetAsync(s.step_counters.p, 0, s.step_counter_bytes, st), "memset");
-    launch_step_kernel(s.step_pg, m.text_linear.wtype, s.step_ctas, st);
-    check_cuda(cudaGetLastError(), "step kernel launch");
-    return;
-  }
   const int d = c.d_model;
   EmbedParams e{};
   e.text_table = m.text_emb.p;
@@ -838,7 +797,7 @@ void enqueue_stt_step(Model& m, State& s, int nb, cudaStream_t st) {
   // Extra (VAD) heads: softmax p[0] of each (stt/model.rs:259-271); never quantised.
   const int eh = m.stt.extra_heads_num, edim = m.stt.extra_heads_dim;
   for (int i = 0; i < eh; i++) {
-    GemvParams h = gemv_base(m.extra[i], s.x.as<float>(), d, nb);
+    GemvParams h = gemv_base(m.extra[i], s.x.as<float>(), d, nb, s);
     set_norm(h, m.out_norm);
     h.epi = EPI_STORE;
     h.out = s.extra_logits.as<float>() + i * edim;
@@ -921,7 +880,7 @@ const GemmOperand& xa_map(State& s, int k, int nb) {
 // and the product runs on the tensor cores.
 void linear_fwd(Model& m, State& s, const Linear& L, const float* x, int64_t x_stride, int nb,
                 int epi, float* out, int64_t out_stride, cudaStream_t st) {
-  GemvParams g = gemv_base(L, x, x_stride, nb);
+  GemvParams g = gemv_base(L, x, x_stride, nb, s);
   g.epi = epi;
   g.out = out;
   g.out_stride = out_stride;
@@ -952,12 +911,12 @@ const float* time_table(Model& m, State& s, int steps, cudaStream_t st) {
       const TimeEmbed& te = m.time_emb[e];
       const float tv = (float)(i + e) / (float)steps;
       launch_time_input(te.freqs.as<float>(), tv, s.temb_in.as<float>(), st);
-      GemvParams g = gemv_base(te.l1, s.temb_in.as<float>(), 256, 1);
+      GemvParams g = gemv_base(te.l1, s.temb_in.as<float>(), 256, 1, s);
       g.epi = EPI_SILU;
       g.out = s.temb_h.as<float>();
       g.out_stride = dim;
       launch_gemv(g, st);
-      g = gemv_base(te.l2, s.temb_h.as<float>(), dim, 1);
+      g = gemv_base(te.l2, s.temb_h.as<float>(), dim, 1, s);
       g.epi = EPI_STORE;
       g.out = s.temb_o.as<float>();
       g.out_stride = dim;

@@ -153,11 +153,14 @@ struct State {
   GemmOperand xa_d[3], xa_q[3], xh_f[3];
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, int> graph_kernels;  // kernel nodes of each captured step graph
-  // The persistent batch-1 step (stepk.cu): its phase program and counters, when it applies.
-  DevBuf step_phases, step_counters, step_part;
-  StepProgram step_pg{};
-  int step_ctas = 0;        // 0: the batch-1 step runs as separate kernels
-  size_t step_counter_bytes = 0;
+  // Reference order (SVL_STATE_REFERENCE_ORDER at creation): every reduction whose
+  // order the reference's CPU path fixes runs in that order -- norm sums element by element,
+  // attention key by key, RoPE from a host table of the C library's cosf / sinf -- so the
+  // step reproduces the reference CPU arithmetic bit for bit; the weight products always
+  // do. The matrix-vector kernels serve every batch size in this mode.
+  bool ref_order = false;
+  DevBuf rope_tab;         // [rope_positions][head_dim / 2] (cos, sin)
+  int rope_positions = 0;
   ~State();
 };
 
@@ -180,7 +183,7 @@ void raise_device_error(State& s, cudaStream_t st);
 // Weight loading (LanguageModel::new / FlowLm::new).
 Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_config* stt,
                     const svl_tts_config* tts, const svl_tensor_view* t, int n, int device);
-State* create_state(Model* m, int max_batch, int max_positions);
+State* create_state(Model* m, int max_batch, int max_positions, uint32_t flags = 0);
 
 // The step kernels for streams [b0, b0 + nb) (no embedding / head).
 void enqueue_layers(Model& m, State& s, int b0, int nb, cudaStream_t st);

@@ -13,6 +13,15 @@ constexpr int kMaxNbChunk = 8;
 // Audio codebooks the embedding kernel stages per stream.
 constexpr int kMaxCodebooks = 127;
 
+// An L2 prefetch of a later kernel's data: every CTA of the kernel that carries it pulls its
+// share of [p, p + bytes) into L2 (cp.async.bulk.prefetch.L2), so the later kernel's reads
+// hit L2 instead of waiting on HBM.
+struct PrefetchRange {
+  const uint8_t* p;
+  int64_t bytes;
+};
+constexpr int kMaxPrefetch = 3;
+
 enum GemvEpilogue {
   EPI_STORE = 0,     // out = acc (+ bias)
   EPI_RESIDUAL = 1,  // out += (acc (+ bias)) * layer_scale
@@ -61,9 +70,17 @@ struct GemvParams {
   unsigned* am_ticket;   // one counter, zero between launches
   uint32_t* tokens;      // [nb] argmax out
   int* pos_advance;      // [nb] positions to advance once the argmax is final, or null
-  // L2 prefetch of a later kernel's weights: each CTA prefetches its share of [pf, pf+pf_bytes).
-  const uint8_t* pf;
-  int64_t pf_bytes;
+  PrefetchRange pf[kMaxPrefetch];  // L2 prefetches of later kernels' data
+  // Reference order (a state option): the norm sums run element by element on one thread,
+  // as on the reference CPU path, instead of as a parallel reduction.
+  int ref_order;
+  // EPI_QKV_ROPE with a cos / sin table: rope_by_pos[pos][i] = (cos, sin)(pos * inv_freq[i])
+  // for pos < rope_positions, evaluated on the host with the C library's cosf / sinf (the
+  // functions the reference's CPU path calls); null = sincosf on the device.
+  const float2* rope_by_pos;
+  int rope_positions;
+  // Set to 2 when a bounded device-side wait runs out (null: not reported).
+  int* err;
 };
 
 void launch_gemv(const GemvParams& p, cudaStream_t s);
@@ -129,6 +146,7 @@ struct AttnParams {
   const unsigned char* kmap;
   const unsigned char* vmap;
   int layer, ring_row0;
+  PrefetchRange pf[kMaxPrefetch];  // L2 prefetches of later kernels' data
 };
 
 void launch_attention_decode(const AttnParams& p, cudaStream_t s);
@@ -138,6 +156,12 @@ int attention_max_splits();
 int attention_piece(int head_dim, int kv_bf16, int ring_cap, int* npieces);
 // Per device, once: raises the dynamic shared-memory limit of the attention kernels.
 void attention_init_device();
+// Decode attention in the reference CPU path's order (attention_ref.cu), for reference-order
+// states: the same inputs and output as launch_attention_decode (splits, pieces and maps are
+// not used). Supported for head_dim 64 / 128 and rings of up to 51,200 keys.
+void launch_attention_ref(const AttnParams& p, cudaStream_t s);
+bool attention_ref_supported(int head_dim, int ring_cap);
+void attention_ref_init_device();
 
 struct EmbedParams {
   const void* text_table;   // [text_card + 1][d]
@@ -156,33 +180,6 @@ void launch_advance_positions(int* pos, int nb, cudaStream_t s);
 // (stream, frequency) per step, shared by every layer's RoPE epilogue.
 void launch_rope_table(const int* pos, int nb, const float* inv_freq, int half, float2* cs,
                        cudaStream_t s);
-
-// The persistent batch-1 step (stepk.cu): the step as a program of phases, each run by every
-// CTA on its share of rows / keys, with a grid-wide counter between phases.
-enum StepPhaseType { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
-struct StepPhase {
-  int type;
-  GemvParams g;   // PH_GEMV (nb = 1)
-  AttnParams a;   // PH_ATTN (nb = 1)
-  EmbedParams e;  // PH_EMBED (nb = 1)
-};
-struct StepProgram {
-  const StepPhase* ph;  // device array
-  int nph;
-  unsigned* done;       // [nph] CTAs that finished each phase, zero at launch
-  unsigned* head_cnt;   // [layers][heads] attention parts merged, zero at launch
-  float* part;          // [heads][splits][head_dim + 2] attention partials
-  int splits;           // key parts per head
-  int slot_bytes, nslots;  // the shared-memory ring
-  int rec_bytes;           // the input record area after the ring
-  int* err;
-};
-constexpr int kStepDynSmem = 208 * 1024;  // ring + input record
-constexpr int kStepRecBytes = 40 * 1024;  // largest input record (f32 k <= 10240)
-// CTAs of the step kernel on this device (one per SM), 0 if it cannot be resident.
-int step_kernel_ctas(int wtype);
-void step_kernel_init_device();
-void launch_step_kernel(const StepProgram& pg, int wtype, int ctas, cudaStream_t s);
 
 // Weight packing: f32 [n][k] (device) into the layout of wtype. interleave_half = F swaps
 // rows so that packed row 2i is source row i and 2i+1 is source row F + i (SwiGLU).

@@ -1,5 +1,6 @@
 // misc.cu — embedding sum, position advance and weight packing.
 #include "common.cuh"
+#include "gemv_common.cuh"
 #include "kernels.cuh"
 #include "sm100.cuh"
 
@@ -84,11 +85,15 @@ __global__ void pack_kernel(const float* src, uint8_t* dst, int64_t row_stride, 
   } else if (wtype == W_Q8) {
     // Q8_0 (ggml; candle QTensor::quantize, nn/mod.rs:81-83): d = amax / 127 stored f16,
     // q = round(x * (1 / d)).
+    // Stored in super-blocks (gemv_common.cuh): element lane of block blk sits in slot lane / 4.
     float amax = warp_max(fabsf(x));
     float d = amax / 127.0f;
     float id = d != 0.0f ? 1.0f / d : 0.0f;
-    reinterpret_cast<int8_t*>(row)[blk * QBLK + lane] = (int8_t)(int)roundf(x * id);
-    if (lane == 0) reinterpret_cast<__half*>(row + k)[blk] = __float2half_rn(d);
+    uint8_t* sb = row + (int64_t)(blk / kSbBlocks) * kQ8SbBytes;
+    const int bj = blk % kSbBlocks;
+    reinterpret_cast<int8_t*>(sb)[(bj >> 2) * 128 + 16 * (lane >> 2) + 4 * (bj & 3) + (lane & 3)] =
+        (int8_t)(int)roundf(x * id);
+    if (lane == 0) reinterpret_cast<__half*>(sb + 256)[bj] = __float2half_rn(d);
   } else {
     // Q4_1 (ggml): d = (max - min) / 15, m = min, q = min(15, trunc((x - min) / d + 0.5)),
     // byte j holds q[j] (low nibble) and q[j + 16] (high nibble).
@@ -103,9 +108,12 @@ __global__ void pack_kernel(const float* src, uint8_t* dst, int64_t row_stride, 
     int q = (int)((x - mn) * id + 0.5f);
     q = q > 15 ? 15 : q;
     int hi = __shfl_down_sync(0xffffffffu, q, 16);
-    if (lane < 16) row[blk * 16 + lane] = (uint8_t)(q | (hi << 4));
+    // Super-block layout (gemv_common.cuh): byte i of block j sits in 4-byte group i / 4.
+    uint8_t* sb = row + (int64_t)(blk / kSbBlocks) * kQ4SbBytes;
+    const int bj = blk % kSbBlocks;
+    if (lane < 16) sb[32 * (lane >> 2) + 4 * bj + (lane & 3)] = (uint8_t)(q | (hi << 4));
     if (lane == 0)
-      reinterpret_cast<__half2*>(row + k / 2)[blk] = __halves2half2(__float2half_rn(d), __float2half_rn(mn));
+      reinterpret_cast<__half2*>(sb + 128)[bj] = __halves2half2(__float2half_rn(d), __float2half_rn(mn));
   }
 }
 
@@ -121,13 +129,17 @@ __global__ void dequant_bf16_kernel(const uint8_t* src, int64_t row_stride, int 
   const int r = (int)(gw / nblk), blk = (int)(gw % nblk);
   const uint8_t* row = src + (int64_t)r * row_stride;
   float x;
+  const int bj = blk % kSbBlocks;
   if (wtype == W_Q8) {
-    const float d = __half2float(reinterpret_cast<const __half*>(row + k)[blk]);
-    x = (float)reinterpret_cast<const int8_t*>(row)[blk * QBLK + lane] * d;
+    const uint8_t* sb = row + (int64_t)(blk / kSbBlocks) * kQ8SbBytes;
+    const float d = __half2float(reinterpret_cast<const __half*>(sb + 256)[bj]);
+    x = (float)reinterpret_cast<const int8_t*>(sb)[(bj >> 2) * 128 + 16 * (lane >> 2) + 4 * (bj & 3) + (lane & 3)] * d;
   } else {
-    const uint8_t b = row[blk * 16 + (lane & 15)];
+    const uint8_t* sb = row + (int64_t)(blk / kSbBlocks) * kQ4SbBytes;
+    const int i = lane & 15;
+    const uint8_t b = sb[32 * (i >> 2) + 4 * bj + (i & 3)];
     const int q = lane < 16 ? (b & 15) : (b >> 4);
-    const float2 dm = __half22float2(reinterpret_cast<const __half2*>(row + k / 2)[blk]);
+    const float2 dm = __half22float2(reinterpret_cast<const __half2*>(sb + 128)[bj]);
     x = dm.x * (float)q + dm.y;
   }
   uint16_t* o = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(dst) + (int64_t)r * dst_stride);
@@ -212,8 +224,8 @@ int64_t packed_row_stride(int wtype, int k) {
   switch (wtype) {
     case W_F32: return pad16((int64_t)k * 4);
     case W_BF16: return pad16((int64_t)k * 2);
-    case W_Q8: return k + pad16((int64_t)(k / QBLK) * 2);
-    default: return k / 2 + pad16((int64_t)(k / QBLK) * 4);
+    case W_Q8: return (int64_t)super_blocks(k) * kQ8SbBytes;
+    default: return (int64_t)super_blocks(k) * kQ4SbBytes;
   }
 }
 

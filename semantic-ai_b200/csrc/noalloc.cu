@@ -27,23 +27,26 @@ constexpr size_t kScratchBytes = 256 + kCandidates * 4 * 2;  // 19,200 bytes
 static __device__ __align__(256) unsigned char g_head_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_once[kMaxDevices];
+std::mutex g_scratch_mu;
 unsigned char* g_scratch_ptr[kMaxDevices];
-cudaError_t g_scratch_err[kMaxDevices];
 
 // The device address of the scratch on `device` (the current device). In host code the
-// array's name is only a host-side stand-in, so the address comes from the runtime, once
-// per device.
+// array's name is only a host-side stand-in, so the address comes from the runtime. It is
+// stored once the lookup succeeds; a failed lookup (for instance one made inside a stream
+// capture) is reported and tried again on the next call.
 unsigned char* scratch_on(int device) {
   if (device < 0 || device >= kMaxDevices) throw Error(SVL_ERR_CUDA, "device index out of range");
-  std::call_once(g_once[device], [device] {
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[device]) {
     void* p = nullptr;
-    g_scratch_err[device] = cudaGetSymbolAddress(&p, g_head_scratch);
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_head_scratch);
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
+      throw Error(SVL_ERR_CUDA, std::string("cudaGetSymbolAddress of the head scratch: ") +
+                                    cudaGetErrorString(e));
+    }
     g_scratch_ptr[device] = static_cast<unsigned char*>(p);
-  });
-  if (g_scratch_err[device] != cudaSuccess || !g_scratch_ptr[device])
-    throw Error(SVL_ERR_CUDA, std::string("cudaGetSymbolAddress of the head scratch: ") +
-                                  cudaGetErrorString(g_scratch_err[device]));
+  }
   return g_scratch_ptr[device];
 }
 

@@ -51,6 +51,18 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
 }
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+// CTA `cta` of `ctas` pulls its 16-byte-aligned share of [base, base + bytes) into L2, in
+// pieces of at most 64 KB.
+__device__ __forceinline__ void prefetch_l2_share(const uint8_t* base, int64_t bytes, int cta, int ctas) {
+  if (!base || bytes <= 0) return;
+  const int64_t share = (bytes / ctas + 15) / 16 * 16;
+  const int64_t a = (int64_t)cta * share;
+  const int64_t e = min(a + share, bytes / 16 * 16);
+  for (int64_t o = a; o < e; o += 65536) prefetch_l2(base + o, (uint32_t)(e - o < 65536 ? e - o : 65536));
+}
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
@@ -68,6 +80,9 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
   uint32_t out;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr(p)), "r"(rank));
   return out;
+}
+__device__ __forceinline__ void dsmem_st(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ float dsmem_ld(uint32_t addr) {
   float v;

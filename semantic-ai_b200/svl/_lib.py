@@ -13,6 +13,8 @@ from .config import CSttConfig, CTensorView, CTransformerConfig, CTtsConfig
 
 LIB_PATH = Path(os.environ.get("SVL_LIB", Path(__file__).resolve().parent.parent / "libsvl_b200.so"))
 
+STATE_REFERENCE_ORDER = 1  # svl_state_create_ex flag (include/svl_cuda.h)
+
 STATUS = {0: "OK", 1: "CONFIG", 2: "INVALID_INPUT", 3: "CUDA", 4: "OOM", 5: "TIMEOUT",
           6: "UNSUPPORTED"}
 
@@ -29,6 +31,7 @@ SIGNATURES = {
     "svl_model_destroy": (None, [_P]),
     "svl_model_weight_bytes": (ctypes.c_int64, [_P]),
     "svl_state_create": (_I, [_P, _I, _I, ctypes.POINTER(_P)]),
+    "svl_state_create_ex": (_I, [_P, _I, _I, ctypes.c_uint32, ctypes.POINTER(_P)]),
     "svl_state_destroy": (None, [_P]),
     "svl_state_reset": (_I, [_P, _I]),
     "svl_state_position": (_I, [_P, _I, ctypes.POINTER(_I)]),

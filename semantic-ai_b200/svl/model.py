@@ -39,9 +39,13 @@ class State:
 
     handle = None
 
-    def __init__(self, model: "_Model", max_batch: int = 1, max_positions: int = 0):
+    def __init__(self, model: "_Model", max_batch: int = 1, max_positions: int = 0,
+                 reference_order: bool = False):
         h = ctypes.c_void_p()
-        _lib.check(_lib.lib().svl_state_create(model.handle, max_batch, max_positions, ctypes.byref(h)))
+        flags = _lib.STATE_REFERENCE_ORDER if reference_order else 0
+        _lib.check(_lib.lib().svl_state_create_ex(model.handle, max_batch, max_positions, flags,
+                                                  ctypes.byref(h)))
+        self.reference_order = reference_order
         self.handle = h
         self.model = model
         self.max_batch = max_batch
@@ -107,9 +111,12 @@ class _Model:
     def weight_bytes(self) -> int:
         return _lib.lib().svl_model_weight_bytes(self.handle)
 
-    def init_state(self, max_batch: int = 1, max_positions: int = 0) -> State:
+    def init_state(self, max_batch: int = 1, max_positions: int = 0,
+                   reference_order: bool = False) -> State:
+        """Transformer::init_state for max_batch streams. reference_order: every reduction in
+        the reference CPU path's order (svl_state_create_ex, SVL_STATE_REFERENCE_ORDER)."""
         self.max_positions_hint = max(self.max_positions_hint, max_positions)
-        return State(self, max_batch, max_positions)
+        return State(self, max_batch, max_positions, reference_order)
 
     def forward(self, xs: np.ndarray, state: State, stream: int = 0) -> np.ndarray:
         """Transformer::forward for one stream: xs [t, d_model] -> [t, d_model]."""

@@ -225,14 +225,17 @@ def test_bad_weights_rejected(svl_lib):
 @pytest.mark.slow
 @pytest.mark.parametrize("wdt", ["f32", "q8_0"])
 def test_stt_1b_256_greedy_steps(svl_lib, oracle_lib, wdt):
-    """Configs 1 and 2: STT-1b, batch 1, 256 greedy steps.
+    """Configs 1 and 2 in a fast (default) state: STT-1b, batch 1, 256 greedy steps.
 
     f32: tokens bit-exact (teacher-forced and free-running), logits within 2e-3.
-    q8_0: at this scale a 1-ulp reduction-order change already moves the oracle's own logits
-    by ~2% (activation quantisation is discontinuous and the random-init network amplifies
-    flips), so the GPU is held to the oracle's self-envelope: per step, the oracle against
-    itself with the RMS-norm sum reversed (teacher-forced on the same tokens). The GPU's
-    median and worst L2-relative deviation must stay within twice that envelope."""
+    q8_0: the north-star bars (256/256 tokens, 2e-2 relative logits) are asserted with
+    equality on reference-order states (test_gpu_reference_order.py). A fast state sums its
+    norms and softmax in parallel and evaluates RoPE with the device's sincosf; the Q8_0
+    activation rounding turns those last-bit differences into different activation blocks,
+    and the random-init network carries them through 16 layers. This test reports how far the
+    fast state lands from the reference (free-running token agreement, first flip, L2-relative
+    logit deviation) and bounds it by the oracle's own sensitivity: the oracle against itself
+    with the RMS-norm sum reversed, teacher-forced on the same tokens."""
     stt = config.stt_1b()
     cfg = stt.transformer(wdt, "f32")
     w = synth.stt_weights(stt, cfg)
@@ -252,12 +255,14 @@ def test_stt_1b_256_greedy_steps(svl_lib, oracle_lib, wdt):
     del om
     gm = LanguageModel(stt, cfg, w)
     del w
+    st = gm.init_state(1)
+    free = gm.run_frames(audio[:, None, :], st)[:, 0]
+    n_free = int(np.sum(free == ref_tok))
+    first = int(np.argmax(free != ref_tok)) if n_free < frames else None
     if wdt == "f32":
         worst, same = teacher_forced(gm, ref_tok, ref_lg, stt, audio, wdt)
-        st = gm.init_state(1)
-        toks = gm.run_frames(audio[:, None, :], st)[:, 0]
-        np.testing.assert_array_equal(toks, ref_tok)
-        print(f"STT-1b f32: worst logit diff {worst:.3g}, {same}/{frames} argmax equal, "
+        np.testing.assert_array_equal(free, ref_tok)
+        print(f"STT-1b f32 fast state: worst logit diff {worst:.3g}, {same}/{frames} argmax equal, "
               f"free-running tokens equal for all {frames} steps")
         return
     st = gm.init_state(1)
@@ -269,9 +274,11 @@ def test_stt_1b_256_greedy_steps(svl_lib, oracle_lib, wdt):
         same += int(tok[0] == ref_tok[i])
         prev = int(ref_tok[i])
     rel = np.array(rel)
-    print(f"STT-1b {wdt}: GPU vs oracle L2-rel median {np.median(rel):.3g} max {rel.max():.3g}, "
-          f"argmax equal {same}/{frames}; oracle self-envelope median {np.median(env):.3g} "
-          f"max {env.max():.3g}, argmax equal {env_same}/{frames}")
+    print(f"STT-1b {wdt} fast state: free-running {n_free}/{frames} tokens equal (first flip at "
+          f"step {first}); teacher-forced L2-relative logit deviation median {np.median(rel):.3g} "
+          f"max {rel.max():.3g} (north-star bar 2e-2), argmax equal {same}/{frames}; oracle "
+          f"self-envelope median {np.median(env):.3g} max {env.max():.3g}, argmax equal "
+          f"{env_same}/{frames}")
     assert np.median(rel) <= 2 * np.median(env) + 1e-3
     assert rel.max() <= 2 * env.max() + 1e-3
     assert same >= env_same - frames // 20

@@ -5,7 +5,8 @@ audio thread that must never enter the allocator) cannot create a state, so it c
 svl_stt_step's head, whose argmax scratch lives in the state. svl_stt_head_noalloc keeps that
 scratch in a fixed array inside the library instead. This checks it, through the C ABI,
 against the head of svl_stt_step on the same hidden states, on two calls in a row (and one
-two-stream call), with the f32 tolerance of the parity tests.
+two-stream call), with the f32 tolerance of the parity tests, for f32 weights and for the
+quantised formats, whose head takes the Q8_0 / Q4_1 branch of the product kernel.
 """
 import ctypes
 
@@ -25,14 +26,15 @@ def _embed(w, stt, text, audio):
     return x
 
 
-def test_head_noalloc_matches_step_head(svl_lib):
+@pytest.mark.parametrize("wdt,kvdt", [("f32", "f32"), ("q8_0", "f32"), ("q4_1", "bf16")])
+def test_head_noalloc_matches_step_head(svl_lib, wdt, kvdt):
     import torch
 
     from svl import LanguageModel, config, synth
     from svl._lib import SvlError, check, lib
 
     stt = config.stt_toy()
-    cfg = stt.transformer("f32")
+    cfg = stt.transformer(wdt, kvdt)
     w = synth.stt_weights(stt, cfg)
     gm = LanguageModel(stt, cfg, w)
     audio = synth.audio_tokens(stt, 2)
