@@ -127,6 +127,12 @@ SVL_API svl_status svl_state_create(svl_model* model, int32_t max_batch, int32_t
  *     positions are limited to max(max_positions, 8192) and rings to 51,200 keys.
  * No counterpart in the reference (whose CPU path is this order). */
 #define SVL_STATE_REFERENCE_ORDER 1u
+/* Testing only, quantised models: a failure drill for the device-side bounded waits. In every
+ * step the first weight product withholds one of its staged weight copies and waits for it
+ * only briefly, so that wait runs out: the kernel records the timeout, lets its other copies
+ * land and returns, and the step reports SVL_ERR_TIMEOUT (svl_state_error for the _device
+ * calls). Nothing faults or hangs; the state's contents after such a step are undefined. */
+#define SVL_STATE_TEST_WITHHELD_COPY 2u
 SVL_API svl_status svl_state_create_ex(svl_model* model, int32_t max_batch, int32_t max_positions,
                                        uint32_t flags, svl_state** out);
 SVL_API void svl_state_destroy(svl_state* state);

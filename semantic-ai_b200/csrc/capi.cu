@@ -109,7 +109,8 @@ SVL_API svl_status svl_state_create_ex(svl_model* model, int32_t max_batch, int3
                                        uint32_t flags, svl_state** out) {
   return guarded([&] {
     need(model && out, SVL_ERR_INVALID_INPUT, "null argument");
-    need((flags & ~SVL_STATE_REFERENCE_ORDER) == 0, SVL_ERR_INVALID_INPUT, "unknown state flags");
+    need((flags & ~(SVL_STATE_REFERENCE_ORDER | SVL_STATE_TEST_WITHHELD_COPY)) == 0, SVL_ERR_INVALID_INPUT,
+         "unknown state flags");
     *out = nullptr;
     svl::State* s = svl::create_state(model->m, max_batch, max_positions, flags);
     *out = new svl_state{s, model};

@@ -378,6 +378,7 @@ State* create_state(Model* m, int max_batch, int max_positions, uint32_t flags) 
     s->cap = s->windowed ? c.context : max_positions;
     if (s->cap <= 0) throw Error(SVL_ERR_INVALID_INPUT, "max_positions must be positive without a window");
     s->ref_order = (flags & SVL_STATE_REFERENCE_ORDER) != 0;
+    s->test_withheld_copy = (flags & SVL_STATE_TEST_WITHHELD_COPY) != 0;
     if (s->ref_order) {
       if (!attention_ref_supported(c.head_dim, s->cap))
         throw Error(SVL_ERR_UNSUPPORTED, "reference order: the ring is too long for the in-order attention");
@@ -538,13 +539,17 @@ void set_norm(GemvParams& p, const Norm& N) {
   p.eps = N.eps;
 }
 
-// L2 prefetches (the small-batch kernels are latency-bound and leave HBM idle between their
-// dependent steps): every kernel of a layer pulls into L2 the data of the kernel two places
-// after it in the chain -- in_proj: out_proj's matrix; attention: linear_in's; out_proj:
-// linear_out's; linear_in: the next layer's in_proj (or the text head); linear_out: the next
-// layer's K and V rings -- and the head pulls layer 0's in_proj and rings for the next step.
-// A range is prefetched only when it takes at most a quarter of L2.
+// L2 prefetches. A small-batch kernel that reads its data cold from HBM gets ~3.5 TB/s (a burst
+// of tens of KB per SM waits ~1.6 us for its first bytes); data prefetched into L2 shortly
+// before comes at ~6-7 TB/s, but is gone again after some 64 MB of other traffic (measured on
+// B200 with bulk copies of 96 KB per SM). So every kernel of the step pulls into L2 the data
+// of the kernel kPrefetchDistance places after it in the step's sequence -- per layer in_proj,
+// attention (the layer's K and V rings), out_proj, linear_in, linear_out, then the STT head --
+// counted cyclically, the next step's first kernels after the head. Measured per STT-1b q8_0
+// step at batch 1: 703 us at distance 2, 708 at 3, 734 at 5 (one layer ahead: evicted before
+// use), 755 at 8. A range is prefetched only when it takes at most a quarter of L2.
 constexpr int64_t kPrefetchMax = 32ll * 1024 * 1024;
+constexpr int kPrefetchDistance = 2;
 
 PrefetchRange weights_range(const Linear* L) {
   if (!L || L->row_stride * L->n > kPrefetchMax) return PrefetchRange{};
@@ -557,6 +562,30 @@ PrefetchRange ring_range(const State& s, int l, int b0, int nb, int v) {
   if (bytes > kPrefetchMax) return PrefetchRange{};
   const DevBuf& r = v ? s.v_ring : s.k_ring;
   return PrefetchRange{r.as<uint8_t>() + ((int64_t)l * s.ring_layer_stride + (int64_t)b0 * s.ring_stream_stride) * s.kv_elt, bytes};
+}
+
+// The prefetches of kernel `idx` of the step (5 per layer: in_proj, attention, out_proj,
+// linear_in, linear_out; then the head of an STT model): the data of kernel
+// idx + kPrefetchDistance.
+void set_prefetch(const Model& m, const State& s, int idx, int b0, int nb, PrefetchRange* pf) {
+  const int L = (int)m.layers.size(), n = 5 * L + (m.kind == 0 ? 1 : 0);
+  const int t = (idx + kPrefetchDistance) % n;
+  for (int i = 0; i < kMaxPrefetch; i++) pf[i] = PrefetchRange{};
+  if (t == 5 * L) {
+    pf[0] = weights_range(&m.text_linear);
+    return;
+  }
+  const Layer& Lt = m.layers[t / 5];
+  switch (t % 5) {
+    case 0: pf[0] = weights_range(&Lt.in_proj); break;
+    case 1:
+      pf[0] = ring_range(s, t / 5, b0, nb, 0);
+      pf[1] = ring_range(s, t / 5, b0, nb, 1);
+      break;
+    case 2: pf[0] = weights_range(&Lt.out_proj); break;
+    case 3: pf[0] = weights_range(&Lt.ff1); break;
+    default: pf[0] = weights_range(&Lt.ff2); break;
+  }
 }
 
 }  // namespace
@@ -612,7 +641,11 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   g.kv_bf16 = s.kv_elt == 2;
   g.rope_by_pos = s.rope_tab.as<float2>();
   g.rope_positions = s.rope_positions;
-  g.pf[0] = weights_range(&L.out_proj);
+  if (l == 0 && s.test_withheld_copy) {
+    g.test_withhold = 1;
+    g.wait_limit = 1u << 12;
+  }
+  set_prefetch(m, s, 5 * l, b0, nb, g.pf);
   lp.in_proj = g;
   // Sliding-window attention (nn/kernels/attention.rs:81-169).
   AttnParams& a = lp.attn;
@@ -640,14 +673,14 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   a.ring_row0 = b0 * c.num_kv_heads * s.cap;
   a.out = attn;
   a.err = s.err.as<int>();
-  a.pf[0] = weights_range(&L.ff1);
+  set_prefetch(m, s, 5 * l + 1, b0, nb, a.pf);
   // out_proj + residual (nn/transformer.rs:344, :239-243).
   g = gemv_base(L.out_proj, attn, qd, nb, s);
   g.epi = EPI_RESIDUAL;
   g.out = x;
   g.out_stride = d;
   g.ls = L.ls1.as<float>();
-  g.pf[0] = weights_range(&L.ff2);
+  set_prefetch(m, s, 5 * l + 2, b0, nb, g.pf);
   lp.out_proj = g;
   // norm2 + feed-forward (nn/transformer.rs:438-464).
   g = gemv_base(L.ff1, x, d, nb, s);
@@ -656,18 +689,14 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   g.out_stride = c.ffn_hidden;
   g.epi = c.ffn_kind == SVL_FFN_GATED_SILU ? EPI_SWIGLU
           : c.ffn_kind == SVL_FFN_PLAIN_GELU_ERF ? EPI_GELU_ERF : EPI_GELU_TANH;
-  const bool last = l + 1 == (int)m.layers.size();
-  g.pf[0] = weights_range(!last ? &m.layers[l + 1].in_proj : m.kind == 0 ? &m.text_linear : nullptr);
+  set_prefetch(m, s, 5 * l + 3, b0, nb, g.pf);
   lp.ff1 = g;
   g = gemv_base(L.ff2, act, c.ffn_hidden, nb, s);
   g.epi = EPI_RESIDUAL;
   g.out = x;
   g.out_stride = d;
   g.ls = L.ls2.as<float>();
-  if (!last) {
-    g.pf[0] = ring_range(s, l + 1, b0, nb, 0);
-    g.pf[1] = ring_range(s, l + 1, b0, nb, 1);
-  }
+  set_prefetch(m, s, 5 * l + 4, b0, nb, g.pf);
   lp.ff2 = g;
   return lp;
 }
@@ -748,10 +777,7 @@ GemvParams head_params(Model& m, State& s, int nb) {
   g.am_idx = s.am_idx.as<int>();
   g.am_ticket = s.am_ticket.as<unsigned>();
   g.tokens = s.tok_out.as<uint32_t>();
-  // The next step starts with layer 0.
-  g.pf[0] = weights_range(&m.layers[0].in_proj);
-  g.pf[1] = ring_range(s, 0, 0, nb, 0);
-  g.pf[2] = ring_range(s, 0, 0, nb, 1);
+  set_prefetch(m, s, 5 * (int)m.layers.size(), 0, nb, g.pf);
   return g;
 }
 

@@ -161,6 +161,7 @@ struct State {
   bool ref_order = false;
   DevBuf rope_tab;         // [rope_positions][head_dim / 2] (cos, sin)
   int rope_positions = 0;
+  bool test_withheld_copy = false;  // SVL_STATE_TEST_WITHHELD_COPY: the bounded-wait drill
   ~State();
 };
 

@@ -367,8 +367,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qgemv_kernel(const GemvP
   uint8_t* xsm = smem + kQHeader;
   uint8_t* stg = xsm + q_records_area(WT, p.k, NB);
 
-  // Group G0 + i into stage i % nst.
+  // Group G0 + i into stage i % nst (the failure drill withholds CTA 0's first copy).
+  const bool withhold = p.test_withhold && blockIdx.x == 0;
+  const uint32_t limit = p.wait_limit ? p.wait_limit : kWaitLimit;
   auto copy_group = [&](int i) {
+    if (withhold && i == 0) return;
     const int g = G0 + i, st = i % nst;
     const uint32_t bytes = (uint32_t)(min(4, p.n - 4 * g) * p.row_stride);
     mbar_expect_tx(&full[st], bytes);
@@ -396,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qgemv_kernel(const GemvP
   int best_i = INT_MAX;
   for (int i = warp; warp < W && i < ng; i += W) {
     const int st = i % nst;
-    if (failed || !mbar_wait(&full[st], (uint32_t)(i / nst) & 1u)) {
+    if (failed || !mbar_wait(&full[st], (uint32_t)(i / nst) & 1u, limit)) {
       if (lane == 0) {
         if (p.err) atomicExch(p.err, 2);
         failed = 1;
@@ -408,6 +411,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qgemv_kernel(const GemvP
     float acc[NB], ms[NB];
 #pragma unroll
     for (int b = 0; b < NB; b++) acc[b] = ms[b] = 0.f;
+#pragma unroll 4
     for (int sb = 0; sb < nsb; sb++) fold_sb<WT, NB>(rowp, sb, nblk, nsb, l, xsm, rec, nb, acc, ms);
     // The stage is read: refill it with the group that comes nst later, which this warp reads
     // next (the refill is ordered after this warp's reads of the stage).

@@ -81,6 +81,10 @@ struct GemvParams {
   int rope_positions;
   // Set to 2 when a bounded device-side wait runs out (null: not reported).
   int* err;
+  // Failure drill (quantised products): CTA 0 withholds its first staged copy and waits at
+  // most wait_limit rounds for it (0: the default limit).
+  int test_withhold;
+  uint32_t wait_limit;
 };
 
 void launch_gemv(const GemvParams& p, cudaStream_t s);

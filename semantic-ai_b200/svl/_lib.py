@@ -13,7 +13,8 @@ from .config import CSttConfig, CTensorView, CTransformerConfig, CTtsConfig
 
 LIB_PATH = Path(os.environ.get("SVL_LIB", Path(__file__).resolve().parent.parent / "libsvl_b200.so"))
 
-STATE_REFERENCE_ORDER = 1  # svl_state_create_ex flag (include/svl_cuda.h)
+STATE_REFERENCE_ORDER = 1  # svl_state_create_ex flags (include/svl_cuda.h)
+STATE_TEST_WITHHELD_COPY = 2
 
 STATUS = {0: "OK", 1: "CONFIG", 2: "INVALID_INPUT", 3: "CUDA", 4: "OOM", 5: "TIMEOUT",
           6: "UNSUPPORTED"}

@@ -40,9 +40,9 @@ class State:
     handle = None
 
     def __init__(self, model: "_Model", max_batch: int = 1, max_positions: int = 0,
-                 reference_order: bool = False):
+                 reference_order: bool = False, flags: int = 0):
         h = ctypes.c_void_p()
-        flags = _lib.STATE_REFERENCE_ORDER if reference_order else 0
+        flags |= _lib.STATE_REFERENCE_ORDER if reference_order else 0
         _lib.check(_lib.lib().svl_state_create_ex(model.handle, max_batch, max_positions, flags,
                                                   ctypes.byref(h)))
         self.reference_order = reference_order
@@ -112,11 +112,12 @@ class _Model:
         return _lib.lib().svl_model_weight_bytes(self.handle)
 
     def init_state(self, max_batch: int = 1, max_positions: int = 0,
-                   reference_order: bool = False) -> State:
+                   reference_order: bool = False, flags: int = 0) -> State:
         """Transformer::init_state for max_batch streams. reference_order: every reduction in
-        the reference CPU path's order (svl_state_create_ex, SVL_STATE_REFERENCE_ORDER)."""
+        the reference CPU path's order (svl_state_create_ex, SVL_STATE_REFERENCE_ORDER); flags:
+        further svl_state_create_ex options."""
         self.max_positions_hint = max(self.max_positions_hint, max_positions)
-        return State(self, max_batch, max_positions, reference_order)
+        return State(self, max_batch, max_positions, reference_order, flags)
 
     def forward(self, xs: np.ndarray, state: State, stream: int = 0) -> np.ndarray:
         """Transformer::forward for one stream: xs [t, d_model] -> [t, d_model]."""
