@@ -157,6 +157,21 @@ SVL_API svl_status svl_state_import(svl_state* state, int32_t stream, int32_t la
                                     const float* k, const float* v, int32_t len,
                                     int32_t position);
 
+/* Voice::save (tts/voice.rs:78-99): stream `stream` of the state as a voice file, in the
+ * safetensors layout of upstream Pocket TTS: per layer i, "transformer.layers.{i}.self_attn/cache"
+ * f32 [2, 1, len, kv_heads, head_dim] (keys then values, oldest first),
+ * ".../offset" i64 [1] = len and ".../pad" i64 [1] = 0. */
+SVL_API svl_status svl_voice_save(svl_state* state, int32_t stream, const char* path);
+
+/* Voice::load (tts/voice.rs:101-149) into streams[0..n_streams) of the state at once: reads a
+ * voice file of that layout (cache f32, bf16 or f16; the length from ".../offset", else the
+ * shape of ".../current_end", else the time axis), refuses padded (batched) states with
+ * SVL_ERR_INVALID_INPUT, uploads the keys and values once and writes them into every listed
+ * stream's ring with one kernel; each stream then continues at position len
+ * (TransformerState::from_layer_caches). */
+SVL_API svl_status svl_voice_load(svl_state* state, const int32_t* streams, int32_t n_streams,
+                                  const char* path);
+
 /* LanguageModel::step (stt/model.rs:239-277) for streams 0..batch-1, host buffers:
  * text_tokens [batch], audio_tokens [batch][n_q] in, out_tokens [batch] (greedy argmax,
  * lowest index on ties) out. out_logits [batch][text_card] and out_extra
@@ -179,6 +194,14 @@ SVL_API svl_status svl_stt_step_device(svl_model* model, svl_state* state, int32
 SVL_API svl_status svl_stt_run_frames(svl_model* model, svl_state* state, int32_t batch,
                                       int32_t n_frames, const uint32_t* audio_tokens,
                                       uint32_t* out_tokens);
+
+/* svl_stt_run_frames that also returns, per frame and stream, the extra (voice activity) heads'
+ * softmax p[0] (Prediction::extra_head_probabilities, stt/model.rs:259-271), the input of
+ * SttEvent::VoiceActivity (stt/mod.rs:566-572): out_extra [n_frames][batch][extra_heads_num]
+ * host memory, or NULL. */
+SVL_API svl_status svl_stt_run_frames_ex(svl_model* model, svl_state* state, int32_t batch,
+                                         int32_t n_frames, const uint32_t* audio_tokens,
+                                         uint32_t* out_tokens, float* out_extra);
 
 /* Transformer::forward (nn/transformer.rs:139-154) of one stream over xs [t][d_model] (host,
  * in place), t >= 1: the prefill path. */

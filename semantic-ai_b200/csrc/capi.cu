@@ -197,6 +197,27 @@ SVL_API svl_status svl_state_import(svl_state* state, int32_t stream, int32_t la
   });
 }
 
+SVL_API svl_status svl_voice_save(svl_state* state, int32_t stream, const char* path) {
+  return guarded([&] {
+    need(state && path, SVL_ERR_INVALID_INPUT, "null argument");
+    svl::State& s = *state->s;
+    check_stream(s, stream);
+    svl::check_cuda(cudaSetDevice(s.m->device), "cudaSetDevice");
+    svl::voice_save(s, stream, path);
+  });
+}
+
+SVL_API svl_status svl_voice_load(svl_state* state, const int32_t* streams, int32_t n_streams,
+                                  const char* path) {
+  return guarded([&] {
+    need(state && path && (n_streams == 0 || streams), SVL_ERR_INVALID_INPUT, "null argument");
+    need(n_streams >= 0, SVL_ERR_INVALID_INPUT, "negative stream count");
+    svl::State& s = *state->s;
+    svl::check_cuda(cudaSetDevice(s.m->device), "cudaSetDevice");
+    svl::voice_load(s, streams, n_streams, path);
+  });
+}
+
 SVL_API svl_status svl_stt_step(svl_model* model, svl_state* state, int32_t batch,
                                 const uint32_t* text_tokens, const uint32_t* audio_tokens,
                                 uint32_t* out_tokens, float* out_logits, float* out_extra) {
@@ -269,6 +290,12 @@ SVL_API svl_status svl_stt_step_device(svl_model* model, svl_state* state, int32
 SVL_API svl_status svl_stt_run_frames(svl_model* model, svl_state* state, int32_t batch,
                                       int32_t n_frames, const uint32_t* audio_tokens,
                                       uint32_t* out_tokens) {
+  return svl_stt_run_frames_ex(model, state, batch, n_frames, audio_tokens, out_tokens, nullptr);
+}
+
+SVL_API svl_status svl_stt_run_frames_ex(svl_model* model, svl_state* state, int32_t batch,
+                                         int32_t n_frames, const uint32_t* audio_tokens,
+                                         uint32_t* out_tokens, float* out_extra) {
   return guarded([&] {
     need(model && state && out_tokens, SVL_ERR_INVALID_INPUT, "null argument");
     svl::Model& m = *model->m;
@@ -295,8 +322,11 @@ SVL_API svl_status svl_stt_run_frames(svl_model* model, svl_state* state, int32_
     svl::check_cuda(cudaSetDevice(m.device), "cudaSetDevice");
     cudaStream_t st = m.stream;
     const size_t fbytes = (size_t)n_frames * batch * nq * 4, obytes = (size_t)n_frames * batch * 4;
+    const int eh = m.stt.extra_heads_num;
+    const size_t ebytes = out_extra && eh > 0 ? (size_t)n_frames * batch * eh * 4 : 0;
     if (s.frames_audio.bytes < fbytes) s.frames_audio.alloc(fbytes);
     if (s.frames_out.bytes < obytes) s.frames_out.alloc(obytes);
+    if (s.frames_extra.bytes < ebytes) s.frames_extra.alloc(ebytes);
     if (nq) svl::check_cuda(cudaMemcpyAsync(s.frames_audio.p, audio.data(), fbytes, cudaMemcpyHostToDevice, st), "h2d");
     // The text token fed at each stream's next step: text_card at position 0, else the
     // stream's last argmax.
@@ -314,8 +344,12 @@ SVL_API svl_status svl_stt_run_frames(svl_model* model, svl_state* state, int32_
       svl::check_cuda(cudaMemcpyAsync(s.tok_in.p, s.tok_out.p, batch * 4, cudaMemcpyDeviceToDevice, st), "copy");
       svl::check_cuda(cudaMemcpyAsync(s.frames_out.as<uint8_t>() + (size_t)f * batch * 4, s.tok_out.p, batch * 4,
                                       cudaMemcpyDeviceToDevice, st), "copy");
+      if (ebytes)
+        svl::check_cuda(cudaMemcpyAsync(s.frames_extra.as<uint8_t>() + (size_t)f * batch * eh * 4, s.extra_p.p,
+                                        (size_t)batch * eh * 4, cudaMemcpyDeviceToDevice, st), "copy");
     }
     svl::check_cuda(cudaMemcpyAsync(out_tokens, s.frames_out.p, obytes, cudaMemcpyDeviceToHost, st), "d2h");
+    if (ebytes) svl::check_cuda(cudaMemcpyAsync(out_extra, s.frames_extra.p, ebytes, cudaMemcpyDeviceToHost, st), "d2h");
     svl::queue_error_read(s, st);
     svl::check_cuda(cudaStreamSynchronize(st), "frames");
     for (int b = 0; b < batch; b++) s.hpos[b] += n_frames;

@@ -129,7 +129,7 @@ struct State {
   DevBuf x, q, attn, act, logits, extra_logits, extra_p;
   DevBuf tok_in, audio_in, tok_out;
   DevBuf am_val, am_idx, am_ticket, err;
-  DevBuf frames_audio, frames_out;  // svl_stt_run_frames
+  DevBuf frames_audio, frames_out, frames_extra;  // svl_stt_run_frames
   // TTS work buffers
   DevBuf latent_in, noise, latent_out, eos, z, y, sy, hbuf, h2buf, modbuf, xs2, tmp;
   DevBuf temb_in, temb_h, temb_o, prompt_tok;
@@ -212,6 +212,9 @@ void set_last_error(const std::string& msg);
 void state_export(State& s, int stream, int layer, float* k, float* v, int* len);
 void state_import(State& s, int stream, int layer, const float* k, const float* v, int len,
                   int position);
+// Voice::save / Voice::load (tts/voice.rs:78-149), voice.cu.
+void voice_save(State& s, int stream, const char* path);
+void voice_load(State& s, const int* streams, int n, const char* path);
 
 }  // namespace svl
 

@@ -39,9 +39,12 @@ SIGNATURES = {
     "svl_state_copy": (_I, [_P, _I, _P, _I]),
     "svl_state_export": (_I, [_P, _I, _I, _F32P, _F32P, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "svl_state_import": (_I, [_P, _I, _I, _F32P, _F32P, _I, _I]),
+    "svl_voice_save": (_I, [_P, _I, ctypes.c_char_p]),
+    "svl_voice_load": (_I, [_P, ctypes.POINTER(_I), _I, ctypes.c_char_p]),
     "svl_stt_step": (_I, [_P, _P, _I, _U32P, _U32P, _U32P, _F32P, _F32P]),
     "svl_stt_step_device": (_I, [_P, _P, _I, _P, _P, _P, _P, _P]),
     "svl_stt_run_frames": (_I, [_P, _P, _I, _I, _U32P, _U32P]),
+    "svl_stt_run_frames_ex": (_I, [_P, _P, _I, _I, _U32P, _U32P, _F32P]),
     "svl_transformer_forward": (_I, [_P, _P, _I, _F32P, _I]),
     "svl_tts_prompt_text": (_I, [_P, _P, _I, _U32P, _I]),
     "svl_tts_prompt_text_batch": (_I, [_P, _P, _I, _U32P, _I]),

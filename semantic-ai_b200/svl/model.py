@@ -85,6 +85,16 @@ class State:
             out.append((k[: np.prod(shape)].reshape(shape), v[: np.prod(shape)].reshape(shape)))
         return out
 
+    def save_voice(self, path, stream: int = 0):
+        """Voice::save (tts/voice.rs:78-99): this stream's KV state as a safetensors voice."""
+        _lib.check(_lib.lib().svl_voice_save(self.handle, stream, str(path).encode()))
+
+    def load_voice(self, path, streams=(0,)):
+        """Voice::load (tts/voice.rs:101-149) into several streams at once."""
+        s = np.ascontiguousarray(streams, np.int32)
+        _lib.check(_lib.lib().svl_voice_load(self.handle, s.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                             s.size, str(path).encode()))
+
     def load_layer_caches(self, caches, position: int, stream: int = 0):
         """TransformerState::from_layer_caches for one stream."""
         for l, (k, v) in enumerate(caches):
@@ -162,15 +172,21 @@ class LanguageModel(_Model):
             res.append(ex)
         return res[0] if len(res) == 1 else tuple(res)
 
-    def run_frames(self, audio: np.ndarray, state: State) -> np.ndarray:
-        """The Recognizer token loop: audio [frames, B, n_q] -> greedy tokens [frames, B]."""
+    def run_frames(self, audio: np.ndarray, state: State, extra: bool = False):
+        """The Recognizer token loop: audio [frames, B, n_q] -> greedy tokens [frames, B] (and,
+        with extra=True, the extra heads' p[0] [frames, B, n_extra])."""
         a = np.ascontiguousarray(audio, np.uint32)
         if a.ndim == 2:
             a = a[:, None, :]
         f, b = a.shape[:2]
         out = np.zeros((f, b), np.uint32)
-        _lib.check(_lib.lib().svl_stt_run_frames(self.handle, state.handle, b, f, _u32(a), _u32(out)))
-        return out
+        if not extra:
+            _lib.check(_lib.lib().svl_stt_run_frames(self.handle, state.handle, b, f, _u32(a), _u32(out)))
+            return out
+        ex = np.zeros((f, b, max(self.stt.extra_heads_num_heads, 1)), np.float32)
+        _lib.check(_lib.lib().svl_stt_run_frames_ex(self.handle, state.handle, b, f, _u32(a), _u32(out),
+                                                    _f32(ex) if self.stt.extra_heads_num_heads else None))
+        return out, ex[:, :, : self.stt.extra_heads_num_heads]
 
 
 class FlowLm(_Model):
