@@ -891,6 +891,7 @@ template <int HD, bool BF16>
 void set_attr() {
   cudaFuncSetAttribute(attn_kernel<HD, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        128 + 2 * kSlots * kTileBytes);
+  cudaFuncSetAttribute(attn_kernel<HD, BF16>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   cudaFuncSetAttribute(attn_warp_kernel<HD, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWSmemLimit);
 }
 
