@@ -276,6 +276,80 @@ SVL_API svl_status svl_step_kernel_count(svl_model* model, svl_state* state, int
 SVL_API svl_status svl_stt_head_noalloc(svl_model* model, int32_t batch, const float* d_hidden,
                                         uint32_t* d_tokens, float* d_logits, void* cuda_stream);
 
+/* ---- Mimi, the codec around the language models (nn/mimi.rs, nn/seanet.rs, nn/conv.rs) ---- */
+
+/* SeanetConfig (nn/seanet.rs:14-30); pad_mode 0 = PadMode::Constant, 1 = Replicate. ratios[0 ..
+ * n_ratios) are the up-sampling ratios from latent to waveform (the encoder uses them reversed). */
+typedef struct svl_seanet_config {
+  int32_t dimension, channels, n_filters, n_residual_layers;
+  int32_t kernel_size, residual_kernel_size, last_kernel_size, dilation_base;
+  int32_t pad_mode, compress, n_ratios;
+  int32_t ratios[8];
+  int32_t _pad;
+} svl_seanet_config;
+/* ProjectedTransformerConfig (nn/mimi.rs:18-29); layer scale is always on (mimi.rs:97). */
+typedef struct svl_projected_transformer_config {
+  int32_t d_model, input_dimension, output_dimension, num_heads, num_layers, context;
+  int32_t dim_feedforward, _pad;
+  double max_period;
+} svl_projected_transformer_config;
+/* MimiConfig (nn/mimi.rs:36-51). parts: SVL_MIMI_ENCODER | SVL_MIMI_DECODER, the halves to
+ * load (the STT path needs only the encoder, the TTS path the decoder). */
+#define SVL_MIMI_ENCODER 1
+#define SVL_MIMI_DECODER 2
+typedef struct svl_mimi_config {
+  int32_t sample_rate, inner_dim, outer_dim, exact_gelu, parts, _pad;
+  double frame_rate;
+  svl_seanet_config encoder, decoder;
+  svl_projected_transformer_config encoder_transformer, decoder_transformer;
+} svl_mimi_config;
+typedef struct svl_mimi svl_mimi;
+typedef struct svl_mimi_state svl_mimi_state;
+typedef struct svl_rvq svl_rvq;
+
+/* MimiEncoder::new / MimiDecoder::new (nn/mimi.rs:140-166, :229-251) on `device`, from f32
+ * tensors named as the reference's load_mimi_weights leaves them (nn/mod.rs:26-52):
+ * "encoder.model.{i}.conv.weight", "encoder_transformer.transformer.layers.{l}...",
+ * "downsample.conv.conv.weight", "upsample.convtr.convtr.weight", "decoder.model.{i}...". */
+SVL_API svl_status svl_mimi_create(const svl_mimi_config* cfg, const svl_tensor_view* tensors,
+                                   int32_t n_tensors, int32_t device, svl_mimi** out);
+SVL_API void svl_mimi_destroy(svl_mimi* mimi);
+/* Audio samples per codec frame (MimiConfig::frame_size, nn/mimi.rs:55-57). */
+SVL_API int32_t svl_mimi_frame_size(const svl_mimi* mimi);
+/* MimiEncoder::init_state and MimiDecoder::init_state (nn/mimi.rs:172-178, :253-259) for
+ * max_batch streams, each call moving at most max_frames codec frames per stream. */
+SVL_API svl_status svl_mimi_state_create(svl_mimi* mimi, int32_t max_batch, int32_t max_frames,
+                                         svl_mimi_state** out);
+SVL_API void svl_mimi_state_destroy(svl_mimi_state* state);
+/* A fresh state for one stream, or every stream when stream < 0. */
+SVL_API svl_status svl_mimi_state_reset(svl_mimi_state* state, int32_t stream);
+/* MimiEncoder::encode_step (nn/mimi.rs:184-191) for streams 0..batch-1, device buffers:
+ * d_pcm [batch][channels][frames * frame_size] in, d_latent [batch][inner_dim][frames] out
+ * (unquantised latents at the codec frame rate), enqueued on cuda_stream (NULL = the codec's
+ * stream). */
+SVL_API svl_status svl_mimi_encode_step_device(svl_mimi* mimi, svl_mimi_state* state,
+                                               int32_t batch, int32_t frames, const float* d_pcm,
+                                               float* d_latent, void* cuda_stream);
+/* MimiDecoder::decode_step (nn/mimi.rs:262-271) for streams 0..batch-1, device buffers:
+ * d_latent [batch][outer_dim][frames] in, d_pcm [batch][channels][frames * frame_size] out. */
+SVL_API svl_status svl_mimi_decode_step_device(svl_mimi* mimi, svl_mimi_state* state,
+                                               int32_t batch, int32_t frames,
+                                               const float* d_latent, float* d_pcm,
+                                               void* cuda_stream);
+/* Quantizer::new (stt/model.rs:92-98): n_q codebooks of `bins` entries from the tensors
+ * "quantizer.rvq_first.input_proj.weight" [256][512][1],
+ * "quantizer.rvq_first.vq.layers.0._codebook.{embedding_sum,cluster_usage}" and the same under
+ * "quantizer.rvq_rest" (layers 0..n_q-2); entries are embedding_sum / max(cluster_usage, 1e-5). */
+SVL_API svl_status svl_rvq_create(int32_t n_q, int32_t bins, const svl_tensor_view* tensors,
+                                  int32_t n_tensors, int32_t device, svl_rvq** out);
+SVL_API void svl_rvq_destroy(svl_rvq* rvq);
+/* Quantizer::encode (stt/model.rs:100-103): d_latent [batch][512][frames] in, d_codes
+ * [batch][frames][n_q] out (nearest entry per codebook, lowest index on ties), device buffers
+ * on cuda_stream (NULL = the quantizer's stream). */
+SVL_API svl_status svl_rvq_encode_device(svl_rvq* rvq, int32_t batch, int32_t frames,
+                                         const float* d_latent, uint32_t* d_codes,
+                                         void* cuda_stream);
+
 /* Message of the last failure on this thread ("" when none). */
 SVL_API const char* svl_last_error(void);
 SVL_API const char* svl_version(void);

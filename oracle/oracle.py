@@ -69,6 +69,22 @@ def lib() -> ctypes.CDLL:
             "orc_f32_to_f16": (ctypes.c_uint16, [F]),
             "orc_f16_to_f32": (F, [ctypes.c_uint16]),
             "orc_round_bf16": (F, [F]),
+            "orc_elu": (F, [F]),
+            "orc_transformer_create": (P, [P, ctypes.c_char_p, ctypes.POINTER(_Tensor), I]),
+            "orc_conv1d_stream": (I, [I, I, I, I, I, I, FP, FP, FP, ctypes.POINTER(I), FP, I, I,
+                                      FP, FP]),
+            "orc_convtr1d_stream": (I, [I, I, I, I, I, FP, FP, FP, FP, I, I, FP]),
+            "orc_mimi_create": (P, [P, ctypes.POINTER(_Tensor), I]),
+            "orc_mimi_free": (None, [P]),
+            "orc_mimi_frame_size": (I, [P]),
+            "orc_mimi_state_create": (P, [P]),
+            "orc_mimi_state_free": (None, [P]),
+            "orc_mimi_encode_step": (I, [P, P, FP, I, FP]),
+            "orc_mimi_decode_step": (I, [P, P, FP, I, FP]),
+            "orc_rvq_create": (P, [I, I, ctypes.POINTER(_Tensor), I]),
+            "orc_rvq_free": (None, [P]),
+            "orc_rvq_encode": (I, [P, FP, I, UP]),
+            "orc_rvq_distances": (I, [P, I, FP, FP]),
         }
         for name, (res, args) in sig.items():
             f = getattr(l, name)
@@ -186,3 +202,131 @@ def greedy_stt(model: OracleModel, audio: np.ndarray, frames: int, state=None,
         logits.append(lg)
         prev = tok if teacher is None else int(teacher[i])
     return np.array(toks, np.uint32), np.stack(logits)
+
+
+def _tensor_array(tensors: dict[str, np.ndarray]):
+    keep = []
+    arr = (_Tensor * len(tensors))()
+    for i, (name, a) in enumerate(tensors.items()):
+        a = np.ascontiguousarray(a, np.float32)
+        nb = name.encode()
+        keep += [a, nb]
+        arr[i] = _Tensor(nb, a.ctypes.data, a.size)
+    return arr, keep
+
+
+def conv1d_stream(w, bias, prev, started, x, stride=1, dilation=1, replicate=False, elu=False,
+                  skip=None):
+    """StreamingConv1d::forward of one stream (nn/conv.rs:122-179): returns the output; prev
+    ([cin][context]) and started (a one-element int32 array) are updated in place."""
+    cout, cin, k = w.shape
+    x = np.ascontiguousarray(x, np.float32)
+    t = x.shape[1]
+    out = np.zeros((cout, t // stride), np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    sk = None if skip is None else np.ascontiguousarray(skip, np.float32)
+    rc = lib().orc_conv1d_stream(cin, cout, k, stride, dilation, int(replicate), fp(w),
+                                 fp(b) if b is not None else None, fp(prev),
+                                 started.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), fp(x), t,
+                                 int(elu), fp(sk) if sk is not None else None, fp(out))
+    if rc:
+        raise ValueError("conv input length is not a positive multiple of the stride")
+    return out
+
+
+def convtr1d_stream(w, bias, partial, x, stride, depthwise=False, elu=False):
+    """StreamingConvTranspose1d::forward of one stream (nn/conv.rs:265-335); partial
+    ([cout][k - stride]) is updated in place."""
+    cin, per, k = w.shape
+    cout = cin if depthwise else per
+    x = np.ascontiguousarray(x, np.float32)
+    t = x.shape[1]
+    out = np.zeros((cout, t * stride), np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    rc = lib().orc_convtr1d_stream(cin, cout, k, stride, int(depthwise), fp(w),
+                                   fp(b) if b is not None else None, fp(partial), fp(x), t,
+                                   int(elu), fp(out))
+    if rc:
+        raise ValueError("invalid transposed convolution")
+    return out
+
+
+class OracleMimi:
+    """MimiEncoder / MimiDecoder (nn/mimi.rs:133-272) for one stream."""
+
+    def __init__(self, cfg, tensors: dict[str, np.ndarray]):
+        self.cfg = cfg
+        arr, self._keep = _tensor_array(tensors)
+        c = cfg.to_c()
+        h = lib().orc_mimi_create(ctypes.byref(c), arr, len(tensors))
+        if not h:
+            raise ValueError("oracle Mimi: missing or mis-shaped tensors")
+        self.handle = h
+        self.frame_size = lib().orc_mimi_frame_size(h)
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib().orc_mimi_free(self.handle)
+            self.handle = None
+
+    def init_state(self):
+        return _MimiState(lib().orc_mimi_state_create(self.handle))
+
+    def encode_step(self, pcm: np.ndarray, state) -> np.ndarray:
+        pcm = np.ascontiguousarray(pcm, np.float32)
+        frames = pcm.shape[-1] // self.frame_size
+        out = np.zeros((self.cfg.inner_dim, frames), np.float32)
+        if lib().orc_mimi_encode_step(self.handle, state.handle, fp(pcm), frames, fp(out)):
+            raise ValueError("oracle encode failed")
+        return out
+
+    def decode_step(self, latent: np.ndarray, state) -> np.ndarray:
+        latent = np.ascontiguousarray(latent, np.float32)
+        frames = latent.shape[-1]
+        out = np.zeros((self.cfg.decoder.channels, frames * self.frame_size), np.float32)
+        if lib().orc_mimi_decode_step(self.handle, state.handle, fp(latent), frames, fp(out)):
+            raise ValueError("oracle decode failed")
+        return out
+
+
+class _MimiState:
+    def __init__(self, handle):
+        self.handle = handle
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib().orc_mimi_state_free(self.handle)
+            self.handle = None
+
+
+class OracleQuantizer:
+    """Quantizer (stt/model.rs:84-170)."""
+
+    def __init__(self, n_q: int, bins: int, tensors: dict[str, np.ndarray]):
+        self.n_q, self.bins = n_q, bins
+        arr, keep = _tensor_array(tensors)
+        h = lib().orc_rvq_create(n_q, bins, arr, len(tensors))
+        if not h:
+            raise ValueError("oracle quantizer: missing or mis-shaped tensors")
+        self.handle = h
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib().orc_rvq_free(self.handle)
+            self.handle = None
+
+    def encode(self, latent: np.ndarray) -> np.ndarray:
+        """latent [512][frames] -> codes [frames][n_q]."""
+        latent = np.ascontiguousarray(latent, np.float32)
+        frames = latent.shape[1]
+        codes = np.zeros((frames, self.n_q), np.uint32)
+        lib().orc_rvq_encode(self.handle, fp(latent), frames, up(codes))
+        return codes
+
+    def distances(self, codebook: int, residual: np.ndarray) -> np.ndarray:
+        r = np.ascontiguousarray(residual, np.float32)
+        d = np.zeros(self.bins, np.float32)
+        lib().orc_rvq_distances(self.handle, codebook, fp(r), fp(d))
+        return d

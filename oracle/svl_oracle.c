@@ -184,6 +184,17 @@ float orc_exp(float x) {
   return x < -87.0f ? 0.0f : y;
 }
 
+/* Activation::Elu (nn/kernels/activation.rs:60-67): x above 0, else 2^k expm1(r) + (2^k - 1)
+ * of x clamped to [-20, 0]. */
+float orc_elu(float x) {
+  if (x != x) return x;
+  if (x > 0.0f) return x;
+  float c = x < -20.0f ? -20.0f : x;
+  float two_k, e;
+  exp_parts(c, &two_k, &e);
+  return fmaf(two_k, e, two_k - 1.0f);
+}
+
 /* Activation::Silu / GeluTanh (nn/kernels/activation.rs:71-83). */
 float orc_silu(float x) { return x / (1.0f + orc_exp(-x)); }
 float orc_gelu_tanh(float x) {
@@ -820,6 +831,27 @@ orc_lm* orc_lm_create(int kind, const orc_tcfg* cfg, const orc_stt_extra* stt,
   wmap w = {tensors, n_tensors};
   int ok = kind == 0 ? build_stt(m, &w) : build_tts(m, &w);
   if (!ok) {
+    orc_lm_free(m);
+    return NULL;
+  }
+  return m;
+}
+
+/* Transformer::new (transformer.rs:106-125) alone, its tensors named under `prefix`: the
+ * transformer of Mimi's ProjectedTransformer (nn/mimi.rs:74-112). */
+orc_lm* orc_transformer_create(const orc_tcfg* cfg, const char* prefix, const orc_tensor* tensors,
+                               int n_tensors) {
+  if (!cfg || !prefix || cfg->d_model <= 0 || cfg->num_layers <= 0 || cfg->num_heads <= 0 ||
+      cfg->num_kv_heads <= 0 || cfg->head_dim <= 0 || cfg->num_heads % cfg->num_kv_heads ||
+      cfg->head_dim % 2) {
+    set_err("invalid transformer config");
+    return NULL;
+  }
+  orc_lm* m = (orc_lm*)calloc(1, sizeof(orc_lm));
+  m->kind = 2;
+  m->cfg = *cfg;
+  wmap w = {tensors, n_tensors};
+  if (!build_transformer(m, &w, prefix)) {
     orc_lm_free(m);
     return NULL;
   }

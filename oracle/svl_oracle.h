@@ -60,6 +60,9 @@ typedef struct orc_state orc_state;
  * bf16 per cfg->weight_dtype. Returns NULL and sets orc_last_error() on failure. */
 orc_lm* orc_lm_create(int kind, const orc_tcfg* cfg, const orc_stt_extra* stt,
                       const orc_tts_extra* tts, const orc_tensor* tensors, int n_tensors);
+/* A bare transformer (kind 2) whose tensors are named under `prefix` (Mimi's transformers). */
+orc_lm* orc_transformer_create(const orc_tcfg* cfg, const char* prefix, const orc_tensor* tensors,
+                               int n_tensors);
 void orc_lm_free(orc_lm*);
 orc_state* orc_state_create(orc_lm*);
 orc_state* orc_state_duplicate(const orc_state*);
@@ -106,6 +109,67 @@ void orc_matvec_q4_1(const float* x, const uint8_t* wblocks, int n, int k, float
 uint16_t orc_f32_to_f16(float x);
 float orc_f16_to_f32(uint16_t h);
 float orc_round_bf16(float x);
+
+/* ---- Mimi codec and residual vector quantizer (svl_codec_oracle.c) ---------------------- */
+
+/* Activation::Elu (nn/kernels/activation.rs:60-67). */
+float orc_elu(float x);
+
+/* Same layouts as svl_seanet_config / svl_projected_transformer_config / svl_mimi_config in
+ * include/svl_cuda.h. */
+typedef struct {
+  int32_t dimension, channels, n_filters, n_residual_layers;
+  int32_t kernel_size, residual_kernel_size, last_kernel_size, dilation_base;
+  int32_t pad_mode, compress, n_ratios;
+  int32_t ratios[8];
+  int32_t _pad;
+} orc_seanet_cfg;
+typedef struct {
+  int32_t d_model, input_dimension, output_dimension, num_heads, num_layers, context;
+  int32_t dim_feedforward, _pad;
+  double max_period;
+} orc_ptrans_cfg;
+typedef struct {
+  int32_t sample_rate, inner_dim, outer_dim, exact_gelu, parts, _pad;
+  double frame_rate;
+  orc_seanet_cfg encoder, decoder;
+  orc_ptrans_cfg encoder_transformer, decoder_transformer;
+} orc_mimi_cfg;
+typedef struct orc_mimi orc_mimi;
+typedef struct orc_mimi_state orc_mimi_state;
+typedef struct orc_rvq orc_rvq;
+
+/* StreamingConv1d::forward (nn/conv.rs:122-179) of one stream, state passed explicitly: w
+ * [cout][cin][k], bias [cout] or NULL, prev [cin][ctx] with ctx = max(0, (k-1) dil + 1 - stride)
+ * and *started (0 before the first chunk; set to 1), x [cin][t] (ELU applied first when elu
+ * is set), skip [cout][t/stride] or NULL (added after the bias), out [cout][t/stride]. */
+int orc_conv1d_stream(int cin, int cout, int k, int stride, int dil, int replicate, const float* w,
+                      const float* bias, float* prev, int* started, const float* x, int t, int elu,
+                      const float* skip, float* out);
+/* StreamingConvTranspose1d::forward (nn/conv.rs:265-335) of one stream: w [cin][cout/groups][k]
+ * (groups 1 or depthwise), partial [cout][k - stride] (zeros at the start), x [cin][t], out
+ * [cout][t * stride]. */
+int orc_convtr1d_stream(int cin, int cout, int k, int stride, int depthwise, const float* w,
+                        const float* bias, float* partial, const float* x, int t, int elu,
+                        float* out);
+
+/* MimiEncoder / MimiDecoder (nn/mimi.rs:133-272) for one stream. */
+orc_mimi* orc_mimi_create(const orc_mimi_cfg* cfg, const orc_tensor* tensors, int n_tensors);
+void orc_mimi_free(orc_mimi*);
+int orc_mimi_frame_size(const orc_mimi*);
+orc_mimi_state* orc_mimi_state_create(orc_mimi*);
+void orc_mimi_state_free(orc_mimi_state*);
+/* pcm [channels][frames * frame_size] -> latent [inner_dim][frames]. */
+int orc_mimi_encode_step(orc_mimi*, orc_mimi_state*, const float* pcm, int frames, float* latent);
+/* latent [outer_dim][frames] -> pcm [channels][frames * frame_size]. */
+int orc_mimi_decode_step(orc_mimi*, orc_mimi_state*, const float* latent, int frames, float* pcm);
+
+/* Quantizer (stt/model.rs:84-170): latent [512][frames] -> codes [frames][n_q]. */
+orc_rvq* orc_rvq_create(int n_q, int bins, const orc_tensor* tensors, int n_tensors);
+void orc_rvq_free(orc_rvq*);
+int orc_rvq_encode(orc_rvq*, const float* latent, int frames, uint32_t* codes);
+/* The distances of one codebook for a residual (test support): dist[bins]. */
+int orc_rvq_distances(orc_rvq*, int codebook, const float* residual, float* dist);
 
 #ifdef __cplusplus
 }

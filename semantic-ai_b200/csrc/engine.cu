@@ -223,7 +223,8 @@ void validate_cfg(const svl_transformer_config& c) {
 }  // namespace
 
 Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_config* stt,
-                    const svl_tts_config* tts, const svl_tensor_view* t, int n, int device) {
+                    const svl_tts_config* tts, const svl_tensor_view* t, int n, int device,
+                    const char* prefix) {
   validate_cfg(cfg);
   int count = 0;
   check_cuda(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
@@ -265,6 +266,10 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
       for (int i = 0; i < stt->extra_heads_num; i++)
         ld.linear(m->extra[i], "extra_heads." + std::to_string(i) + ".weight", "",
                   stt->extra_heads_dim, d, false);
+    } else if (kind == 2) {
+      // A bare Transformer::new (nn/transformer.rs:106-125) under `prefix`: the transformer
+      // of Mimi's ProjectedTransformer (nn/mimi.rs:74-112), no embedding and no head.
+      ld.transformer(prefix ? prefix : "transformer.");
     } else {
       // FlowLm::new (tts/flow_lm.rs:45-126), english config: no z_proj, no low-rank table.
       if (!tts) throw Error(SVL_ERR_CONFIG, "missing TTS config");

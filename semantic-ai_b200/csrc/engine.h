@@ -88,7 +88,7 @@ struct ResBlock {
 };
 
 struct Model {
-  int kind = 0;  // 0 STT LanguageModel, 1 Pocket-TTS FlowLm
+  int kind = 0;  // 0 STT LanguageModel, 1 Pocket-TTS FlowLm, 2 bare transformer
   int device = 0;
   svl_transformer_config cfg{};
   svl_stt_config stt{};
@@ -182,8 +182,11 @@ void queue_error_read(State& s, cudaStream_t st);
 void raise_device_error(State& s, cudaStream_t st);
 
 // Weight loading (LanguageModel::new / FlowLm::new).
+// kind 0 STT LanguageModel, 1 Pocket-TTS FlowLm, 2 a bare transformer whose tensors are
+// named under `prefix` (Mimi's transformers).
 Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_config* stt,
-                    const svl_tts_config* tts, const svl_tensor_view* t, int n, int device);
+                    const svl_tts_config* tts, const svl_tensor_view* t, int n, int device,
+                    const char* prefix = nullptr);
 State* create_state(Model* m, int max_batch, int max_positions, uint32_t flags = 0);
 
 // The step kernels for streams [b0, b0 + nb) (no embedding / head).

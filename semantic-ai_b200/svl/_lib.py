@@ -54,6 +54,17 @@ SIGNATURES = {
     "svl_step_kernel_count": (_I, [_P, _P, _I, ctypes.POINTER(ctypes.c_int32)]),
     "svl_state_error": (_I, [_P]),
     "svl_stt_head_noalloc": (_I, [_P, _I, _P, _P, _P, _P]),
+    "svl_mimi_create": (_I, [_P, _P, _I, _I, ctypes.POINTER(_P)]),
+    "svl_mimi_destroy": (None, [_P]),
+    "svl_mimi_frame_size": (_I, [_P]),
+    "svl_mimi_state_create": (_I, [_P, _I, _I, ctypes.POINTER(_P)]),
+    "svl_mimi_state_destroy": (None, [_P]),
+    "svl_mimi_state_reset": (_I, [_P, _I]),
+    "svl_mimi_encode_step_device": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "svl_mimi_decode_step_device": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "svl_rvq_create": (_I, [_I, _I, _P, _I, _I, ctypes.POINTER(_P)]),
+    "svl_rvq_destroy": (None, [_P]),
+    "svl_rvq_encode_device": (_I, [_P, _I, _I, _P, _P, _P]),
     "svl_last_error": (ctypes.c_char_p, []),
     "svl_version": (ctypes.c_char_p, []),
 }

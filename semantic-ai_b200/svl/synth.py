@@ -134,3 +134,128 @@ def audio_tokens(stt: SttConfig, frames: int, seed: int = 1, streams: int | None
     for s in range(streams):
         out[:, s] = np.random.default_rng(seed + s).integers(0, stt.card, size=(frames, stt.n_q), dtype=np.uint32)
     return out
+
+
+# ------------------------------------------------------------------ Mimi and the quantizer
+
+def _conv_spec(prefix: str, cin: int, cout: int, k: int, bias: bool = True):
+    out = [(prefix + ".weight", (cout, cin, k), ("fan", cin * k))]
+    if bias:
+        out.append((prefix + ".bias", (cout,), "w"))
+    return out
+
+
+def _resnet_spec(prefix: str, dim: int, seanet):
+    hidden = dim // seanet.compress
+    return (_conv_spec(prefix + ".block.1.conv", dim, hidden, seanet.residual_kernel_size)
+            + _conv_spec(prefix + ".block.3.conv", hidden, dim, 1))
+
+
+def _ptrans_spec(prefix: str, p):
+    from .config import FFN_PLAIN_GELU_ERF, NORM_LAYER, TransformerConfig
+    cfg = TransformerConfig(d_model=p.d_model, num_layers=p.num_layers, num_heads=p.num_heads,
+                            num_kv_heads=p.num_heads, head_dim=p.d_model // p.num_heads,
+                            ffn_kind=FFN_PLAIN_GELU_ERF, ffn_hidden=p.dim_feedforward,
+                            norm_kind=NORM_LAYER, norm_eps=1e-5, layer_scale=True)
+    out = [(n.replace(".in_proj.weight", ".in_proj_weight"), s, k)
+           for n, s, k in transformer_specs(cfg, prefix + ".transformer.")]
+    if p.input_dimension != p.d_model:
+        out.append((prefix + ".input_proj.weight", (p.d_model, p.input_dimension, 1), ("fan", p.input_dimension)))
+    if p.output_dimension != p.d_model:
+        out.append((prefix + ".output_projs.0.weight", (p.output_dimension, p.d_model, 1), ("fan", p.d_model)))
+    return out
+
+
+def mimi_specs(cfg):
+    """Tensor names of MimiEncoder::new / MimiDecoder::new (nn/mimi.rs:140-166, :229-251) after
+    load_mimi_weights' renaming (nn/mod.rs:26-52). Convolutions are N(0, 1 / fan_in) so that
+    activations keep their scale through the SEANet stacks."""
+    from .codec import DECODER, ENCODER
+    out = []
+    if cfg.parts & ENCODER:
+        s, li, mult = cfg.encoder, 0, 1
+        out += _conv_spec(f"encoder.model.{li}.conv", s.channels, s.n_filters, s.kernel_size)
+        li += 1
+        for r in reversed(s.ratios):
+            dim = mult * s.n_filters
+            for _ in range(s.n_residual_layers):
+                out += _resnet_spec(f"encoder.model.{li}", dim, s)
+                li += 1
+            li += 1
+            out += _conv_spec(f"encoder.model.{li}.conv", dim, 2 * dim, 2 * r)
+            li += 1
+            mult *= 2
+        li += 1
+        out += _conv_spec(f"encoder.model.{li}.conv", mult * s.n_filters, s.dimension, s.last_kernel_size)
+        out += _ptrans_spec("encoder_transformer", cfg.encoder_transformer)
+        st = cfg.resample_stride(s)
+        if st > 1:
+            out += _conv_spec("downsample.conv.conv", cfg.encoder_transformer.output_dimension,
+                              cfg.inner_dim, 2 * st, bias=False)
+    if cfg.parts & DECODER:
+        s = cfg.decoder
+        st = cfg.resample_stride(s)
+        if st > 1:
+            out.append(("upsample.convtr.convtr.weight", (cfg.outer_dim, 1, 2 * st), ("fan", 2)))
+        out += _ptrans_spec("decoder_transformer", cfg.decoder_transformer)
+        mult, li = 1 << len(s.ratios), 0
+        out += _conv_spec(f"decoder.model.{li}.conv", s.dimension, mult * s.n_filters, s.kernel_size)
+        li += 1
+        for r in s.ratios:
+            dim = mult * s.n_filters
+            li += 1
+            out += [(f"decoder.model.{li}.convtr.weight", (dim, dim // 2, 2 * r), ("fan", dim * 2)),
+                    (f"decoder.model.{li}.convtr.bias", (dim // 2,), "w")]
+            li += 1
+            for _ in range(s.n_residual_layers):
+                out += _resnet_spec(f"decoder.model.{li}", dim // 2, s)
+                li += 1
+            mult //= 2
+        li += 1
+        out += _conv_spec(f"decoder.model.{li}.conv", s.n_filters, s.channels, s.last_kernel_size)
+    return out
+
+
+def rvq_specs(n_q: int, bins: int):
+    """Quantizer::new's tensors (stt/model.rs:92-157): input projections [256][512][1], and per
+    codebook embedding_sum [bins][256] (N(0, 1) times the usage) and cluster_usage [bins] (uniform
+    in [0.5, 2], one entry of the first codebook below the 1e-5 floor)."""
+    out = [("quantizer.rvq_first.input_proj.weight", (256, 512, 1), ("fan", 512))]
+    if n_q > 1:
+        out.append(("quantizer.rvq_rest.input_proj.weight", (256, 512, 1), ("fan", 512)))
+    for k in range(n_q):
+        pre = ("quantizer.rvq_first.vq.layers.0._codebook." if k == 0
+               else f"quantizer.rvq_rest.vq.layers.{k - 1}._codebook.")
+        out += [(pre + "embedding_sum", (bins, 256), "embsum"), (pre + "cluster_usage", (bins,), "usage")]
+    return out
+
+
+def materialize_codec(specs, seed: int = 0, std: float = 0.02) -> dict[str, np.ndarray]:
+    """materialize() with the codec kinds: ("fan", n) is N(0, 1 / n); "usage" uniform in
+    [0.5, 2]; "embsum" N(0, 1) scaled by the matching usage row."""
+    out = {}
+    for name, shape, kind in specs:
+        if isinstance(kind, tuple) and kind[0] == "fan":
+            out[name] = _normal(seed, name, shape, 1.0 / math.sqrt(kind[1]))
+        elif kind == "usage":
+            u = tensor_rng(seed, name).uniform(0.5, 2.0, size=shape).astype(np.float32)
+            if name.startswith("quantizer.rvq_first"):
+                u[3] = 1e-7  # below the floor of Codebook::new
+            out[name] = u
+        elif kind == "embsum":
+            out[name] = _normal(seed, name, shape, 1.0)
+        else:
+            out.update(materialize([(name, shape, kind)], seed, std, threads=1))
+    for name in list(out):
+        if name.endswith("embedding_sum"):
+            usage = out[name[: -len("embedding_sum")] + "cluster_usage"]
+            out[name] = (out[name] * np.maximum(usage, 1e-5)[:, None]).astype(np.float32)
+    return out
+
+
+def mimi_weights(cfg, seed: int = 0):
+    return materialize_codec(mimi_specs(cfg), seed)
+
+
+def rvq_weights(n_q: int, bins: int, seed: int = 0):
+    return materialize_codec(rvq_specs(n_q, bins), seed)
