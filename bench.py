@@ -49,6 +49,9 @@ CONFIGS = {
                wdt="q4_1", kv="bf16", batch=128, frames=1500, stagger=375),
     "5": dict(workload="pocket-tts bf16 512 streams/GPU, 64-token prompts (BASELINE config 5)",
               kind="tts", wdt="bf16", kv="bf16", batch=512, frames=500, prompt=64),
+    "codec": dict(workload="codec: STT Mimi encoder + 32-codebook RVQ, and Pocket-TTS Mimi decoder, "
+                           "64 streams/GPU, one 80 ms frame per stream per step",
+                  kind="codec", wdt="f32", kv="f32", batch=64, frames=100),
 }
 
 
@@ -537,6 +540,162 @@ def run_tts(args, spec, rank, world, local_rank):
         print(json.dumps(out), flush=True)
 
 
+def codec_flops(cfg, part) -> int:
+    """Multiply-adds x 2 of one codec frame of one stream: every convolution, the transformer's
+    products and attention at its window, and (encoder) the quantizer's 32 x 2048 distances."""
+    from svl import codec
+    fl = 0
+    fs = cfg.frame_size
+    if part == codec.ENCODER:
+        s, t, mult = cfg.encoder, fs, 1
+        fl += 2 * s.n_filters * s.channels * s.kernel_size * t
+        for r in reversed(s.ratios):
+            dim = mult * s.n_filters
+            fl += s.n_residual_layers * 2 * t * (dim * (dim // s.compress) * (s.residual_kernel_size + 1))
+            t //= r
+            fl += 2 * (2 * dim) * dim * 2 * r * t
+            mult *= 2
+        fl += 2 * s.dimension * mult * s.n_filters * s.last_kernel_size * t
+        p = cfg.encoder_transformer
+        fl += t * 2 * p.num_layers * (4 * p.d_model * p.d_model + 2 * p.d_model * p.dim_feedforward
+                                      + 2 * p.d_model * p.context)
+        st = cfg.resample_stride(s)
+        fl += 2 * cfg.inner_dim * p.output_dimension * 2 * st * (t // st)
+        fl += 2 * (2 * 256 * 512 + 32 * 2048 * 256)
+    else:
+        s = cfg.decoder
+        st = cfg.resample_stride(s)
+        fl += 2 * s.dimension * 2 * st  # depthwise up-sampling of one latent frame
+        t = st
+        p = cfg.decoder_transformer
+        fl += t * 2 * p.num_layers * (4 * p.d_model * p.d_model + 2 * p.d_model * p.dim_feedforward
+                                      + 2 * p.d_model * p.context)
+        mult = 1 << len(s.ratios)
+        fl += 2 * mult * s.n_filters * s.dimension * s.kernel_size * t
+        for r in s.ratios:
+            dim = mult * s.n_filters
+            fl += 2 * dim * (dim // 2) * 2 * r * t
+            t *= r
+            h = dim // 2
+            fl += s.n_residual_layers * 2 * t * (h * (h // s.compress) * (s.residual_kernel_size + 1))
+            mult //= 2
+        fl += 2 * s.channels * s.n_filters * s.last_kernel_size * t
+    return int(fl)
+
+
+def run_codec(args, spec, rank, world, local_rank):
+    """The codec on both sides of the LMs, one codec frame (80 ms) of every stream per step: the
+    STT Mimi encoder followed by the quantizer (audio -> the LM's 32 audio tokens, stt/mod.rs:
+    532-541), and the Pocket-TTS Mimi decoder (latents -> audio, tts/mod.rs:441-447). f32 on the
+    CUDA cores; the roofline is the FP32 FMA rate (nominal: SMs x 128 lanes x 2 x max clock)."""
+    import torch
+    import oracle
+    from svl import codec
+
+    torch.cuda.set_device(local_rank)
+    dist = init_dist(world, local_rank)
+    B, K, W = spec["batch"], args.steps, args.warmup
+    peaks, src = load_peaks()
+    props = torch.cuda.get_device_properties(local_rank)
+    fp32_peak = props.multi_processor_count * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
+    stream = torch.cuda.Stream()
+    out = {"metric": "stream-frames/s", "unit": "stream-frames/s", "n_gpus": world, "steps": K,
+           "warmup": W, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "f32", "data": "synthetic (random-init weights seed 0, N(0, 0.09) audio seed 11+rank)",
+           "config": {"workload": spec["workload"], "streams_per_gpu": B,
+                      "inputs": "one frame per step, distinct per step; 1.1 GB of inputs per leg > L2"}}
+    legs = {}
+    for part, name in ((codec.ENCODER, "encoder+rvq"), (codec.DECODER, "decoder")):
+        cfg = codec.stt_mimi(codec.ENCODER) if part == codec.ENCODER else codec.tts_mimi(codec.DECODER)
+        w = synth.mimi_weights(cfg)
+        if part == codec.ENCODER:
+            w.update(synth.rvq_weights(32, 2048))
+        m = codec.Mimi(cfg, w)
+        q = codec.Quantizer(32, 2048, w) if part == codec.ENCODER else None
+        st = m.init_state(B, 1)
+        fs = m.frame_size
+        g = torch.Generator(device="cuda").manual_seed(11 + rank)
+        n_in = min(K + W, 16)
+        if part == codec.ENCODER:
+            ins = [0.3 * torch.randn((B, 1, fs), generator=g, device="cuda") for _ in range(n_in)]
+        else:
+            ins = [torch.randn((B, cfg.outer_dim, 1), generator=g, device="cuda") for _ in range(n_in)]
+
+        def step(i):
+            if part == codec.ENCODER:
+                return q.encode(m.encode_step(ins[i % n_in], st, stream), stream)
+            return m.decode_step(ins[i % n_in], st, stream)
+
+        with torch.cuda.stream(stream):
+            for i in range(W):
+                step(i)
+            stream.synchronize()
+            if dist:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(K):
+                step(W + i)
+            e1.record(stream)
+            e1.synchronize()
+        ms = e0.elapsed_time(e1) / K
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        # End to end: the frame from pinned host memory, the result back to the host.
+        host_in = [x.cpu().pin_memory() for x in ins[:4]]
+        h2d = host_in[0].numel() * 4
+        with torch.cuda.stream(stream):
+            res = step(0)
+            d2h = res.numel() * res.element_size()
+            stream.synchronize()
+            t0 = time.perf_counter()
+            for i in range(K):
+                x = host_in[i % 4].to("cuda", non_blocking=True)
+                y = (q.encode(m.encode_step(x, st, stream), stream) if part == codec.ENCODER
+                     else m.decode_step(x, st, stream))
+                y.cpu()
+            stream.synchronize()
+            e2e_ms = (time.perf_counter() - t0) * 1e3 / K
+        flops = codec_flops(cfg, part) * B
+        leg = {"value": round(B * world * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+               "e2e": {"value": round(B * world * 1e3 / e2e_ms, 1), "unit": "stream-frames/s",
+                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+               "roofline": {"bound": "fp32", "achieved": round(flops / (ms * 1e-3) / 1e12, 2),
+                            "peak": round(fp32_peak, 1), "unit": "TFLOP/s",
+                            "frac": round(flops / (ms * 1e-3) / 1e12 / fp32_peak, 4),
+                            "peak_source": "nominal FP32 FMA rate (SMs x 128 x 2 x max SM clock)",
+                            "flops_per_step": flops}}
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            om = oracle.OracleMimi(cfg, w)
+            oq = oracle.OracleQuantizer(32, 2048, w) if part == codec.ENCODER else None
+            os_ = om.init_state()
+            x = ins[0][0].cpu().numpy()
+            n, t0 = 0, time.perf_counter()
+            while time.perf_counter() - t0 < min(args.cpu_seconds, 10.0):
+                if part == codec.ENCODER:
+                    oq.encode(om.encode_step(x, os_))
+                else:
+                    om.decode_step(x, os_)
+                n += 1
+            v = n / (time.perf_counter() - t0)
+            leg["cpu_baseline"] = {"value": round(v, 3), "unit": "stream-frames/s", "cores": os.cpu_count(),
+                                   "kind": "port", "sample": f"{n} frames of one stream"}
+        legs[name] = leg
+        del m, q, st
+    out.update(value=legs["encoder+rvq"]["value"], ms_per_step=legs["encoder+rvq"]["ms_per_step"],
+               e2e=legs["encoder+rvq"]["e2e"], roofline=legs["encoder+rvq"]["roofline"],
+               decoder=legs["decoder"])
+    if "cpu_baseline" in legs["encoder+rvq"]:
+        out["cpu_baseline"] = legs["encoder+rvq"]["cpu_baseline"]
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 def cpu_baseline_tts(cfg, tts, weights, prompt, budget_s=15.0, frames_cap=None):
     """The oracle's FlowLm step on the host's cores: stream 0's prompt, then frames until the
     time budget is spent."""
@@ -584,6 +743,33 @@ def run_reference(args, spec, rank):
     """The reference's CPU implementation of the path: the oracle port (the Rust reference
     cannot be built in this image), all host threads, bounded samples of the workload."""
     if rank != 0:
+        return
+    if spec.get("kind") == "codec":
+        # The STT Mimi encoder + quantizer of one stream on the oracle port, frame after frame.
+        import oracle as O
+        from svl import codec
+        O.set_threads(os.cpu_count() or 1)
+        cfg = codec.stt_mimi(codec.ENCODER)
+        w = synth.mimi_weights(cfg)
+        w.update(synth.rvq_weights(32, 2048))
+        om, oq = O.OracleMimi(cfg, w), O.OracleQuantizer(32, 2048, w)
+        st = om.init_state()
+        pcm = (0.3 * np.random.default_rng(11).standard_normal((1, om.frame_size))).astype(np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < min(args.ref_seconds, 30.0) and n < args.steps + args.warmup:
+            oq.encode(om.encode_step(pcm, st))
+            n += 1
+        value = round(n / (time.perf_counter() - t0), 3)
+        cb = {"value": value, "unit": "stream-frames/s", "cores": os.cpu_count(), "kind": "port",
+              "sample": f"{n} frames of one stream (C restatement of the reference CPU path)"}
+        print(json.dumps({"metric": "stream-frames/s", "value": value, "unit": "stream-frames/s",
+                          "n_gpus": args.gpus, "steps": n, "warmup": 0,
+                          "ms_per_step": round(1e3 / max(value, 1e-9), 3), "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                          "config": {"workload": spec["workload"], "streams_per_gpu": spec["batch"]},
+                          "impl": "reference", "cpu_baseline": cb,
+                          "e2e": {"value": value, "unit": "stream-frames/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
         return
     if spec.get("kind") == "tts":
         cfg, tts = tts_config(spec)
@@ -687,6 +873,8 @@ def main():
         run_reference(args, spec, rank)
     elif spec.get("kind") == "tts":
         run_tts(args, spec, rank, world, local_rank)
+    elif spec.get("kind") == "codec":
+        run_codec(args, spec, rank, world, local_rank)
     else:
         run_ours(args, spec, rank, world, local_rank)
 
