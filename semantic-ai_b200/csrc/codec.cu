@@ -81,7 +81,7 @@ struct ConvArgs {
   const int* started;  // [stream]: 0 before the stream's first chunk
   int b0, ctx;
   int cin, cout, k, stride, dil, act, replicate;
-  const float* w;     // [cout][cin][k]
+  const float* w;     // transposed: [cin * k][cout]
   const float* bias;  // [cout] or null
   const float* skip;  // resnet skip [b][cout][len] with the output's strides, or null
   float* out;         // [b][cout][len]
@@ -101,55 +101,74 @@ __device__ __forceinline__ float conv_in(const ConvArgs& a, int b, int c, int i,
   return a.act == ACT_ELU ? elu_ref(v) : v;
 }
 
-// CTA tile: TO output channels x TL output times of one stream; thread (o, g) computes times
-// 4g .. 4g + 3 of channel o. Chunks of CC input channels are staged: the weights [TO][CC * k]
-// (rows padded to an odd word count, so the 32 channels of a warp hit distinct banks) and the
-// input window they need [CC][xs]; a warp's lanes share one time group, so input reads are
-// broadcasts.
-template <int TL>
-__global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvArgs a, int cc_max, int wrow, int xs) {
-  constexpr int TO = kConvThreads * 4 / TL;
-  extern __shared__ float sm[];
-  float* ws = sm;                   // [TO][wrow]
-  float* xsm = sm + TO * wrow;      // [cc_max][xs]
-  const int b = blockIdx.z, o0 = blockIdx.y * TO, l0 = blockIdx.x * TL;
-  const int tid = threadIdx.x, ol = tid % TO, g = tid / TO;
-  const bool started = a.started[a.b0 + b] != 0;
+// CTA tile: 64 output channels x 64 columns, a column being one output time of one stream
+// (column q = stream q / len, time q % len: short chunks of many streams share one tile, so a
+// staged weight serves every stream of it). 256 threads in a 16 x 16 grid, each computing a
+// 4 x 4 register block (channels o..o+3, columns q..q+3). Chunks of input channels are staged
+// in shared memory as im2col rows, both operands [channel * k + tap][64]: the weights from the
+// layer's transposed copy [cin * k][cout] and the inputs gathered per column from
+// [carried context | act(chunk)]; the inner loop reads one float4 of each for 16 FMAs. Every
+// output is one FMA chain over (channel, tap) in order.
+constexpr int kConvTile = 64;
+
+__global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvArgs a, int cc_max, int nb) {
+  constexpr int T = kConvTile, G = T / 4;
+  extern __shared__ __align__(16) float sm[];
+  float* ws = sm;                      // [cc_max * k][T]
+  float* xsm = sm + cc_max * a.k * T;  // [cc_max * k][T]
+  const int o0 = blockIdx.y * T, q0 = blockIdx.x * T, ncol = nb * a.len;
+  const int tid = threadIdx.x, og = tid % G, cg = tid / G;
   const int total = a.ctx + a.t;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; u++)
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc[u][i] = 0.f;
   for (int c0 = 0; c0 < a.cin; c0 += cc_max) {
     const int cc = min(cc_max, a.cin - c0), ck = cc * a.k;
     __syncthreads();
-    for (int i = tid; i < TO * ck; i += kConvThreads) {
-      const int o = i / ck, r = i - o * ck;
-      ws[o * wrow + r] = o0 + o < a.cout ? a.w[((int64_t)(o0 + o) * a.cin + c0) * a.k + r] : 0.f;
+    for (int i = tid; i < ck * T; i += kConvThreads) {
+      const int r = i / T, o = i - r * T;
+      ws[i] = o0 + o < a.cout ? a.w[((int64_t)c0 * a.k + r) * a.cout + o0 + o] : 0.f;
     }
-    for (int i = tid; i < cc * xs; i += kConvThreads) {
-      const int c = i / xs, u = i - c * xs, pos = l0 * a.stride + u;
-      xsm[c * xs + u] = pos < total ? conv_in(a, b, c0 + c, pos, started) : 0.f;
+    for (int i = tid; i < ck * T; i += kConvThreads) {
+      const int r = i / T, col = i - r * T, q = q0 + col;
+      float v = 0.f;
+      if (q < ncol) {
+        const int b = q / a.len, l = q - b * a.len, c = r / a.k, j = r - c * a.k;
+        const int pos = l * a.stride + j * a.dil;
+        if (pos < total) v = conv_in(a, b, c0 + c, pos, a.started[a.b0 + b] != 0);
+      }
+      xsm[i] = v;
     }
     __syncthreads();
-    const float* wr = ws + ol * wrow;
-    const float* xb = xsm + (4 * g) * a.stride;
-    for (int c = 0; c < cc; c++)
-      for (int j = 0; j < a.k; j++) {
-        const float wv = wr[c * a.k + j];
-        const float* xp = xb + c * xs + j * a.dil;
+    const float* wb = ws + 4 * og;
+    const float* xb = xsm + 4 * cg;
+    for (int r = 0; r < ck; r++) {
+      const float4 w4 = *reinterpret_cast<const float4*>(wb + r * T);
+      const float4 x4 = *reinterpret_cast<const float4*>(xb + r * T);
+      const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, xv[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
-        for (int i = 0; i < 4; i++) acc[i] = fmaf(wv, xp[i * a.stride], acc[i]);
-      }
+      for (int u = 0; u < 4; u++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[u][i] = fmaf(wv[u], xv[i], acc[u][i]);
+    }
   }
-  const int o = o0 + ol;
-  if (o >= a.cout) return;
 #pragma unroll
   for (int i = 0; i < 4; i++) {
-    const int l = l0 + 4 * g + i;
-    if (l >= a.len) continue;
-    float v = acc[i];
-    if (a.bias) v = __fadd_rn(v, a.bias[o]);  // matmul, then broadcast_add of the bias
-    const int64_t off = b * a.o_bs + (int64_t)o * a.o_cs + l;
-    if (a.skip) v = __fadd_rn(a.skip[off], v);  // ResnetBlock: xs + ys
-    a.out[off] = v;
+    const int q = q0 + 4 * cg + i;
+    if (q >= ncol) continue;
+    const int b = q / a.len, l = q - b * a.len;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int o = o0 + 4 * og + u;
+      if (o >= a.cout) continue;
+      float v = acc[u][i];
+      if (a.bias) v = __fadd_rn(v, a.bias[o]);  // matmul, then broadcast_add of the bias
+      const int64_t off = b * a.o_bs + (int64_t)o * a.o_cs + l;
+      if (a.skip) v = __fadd_rn(a.skip[off], v);  // ResnetBlock: xs + ys
+      a.out[off] = v;
+    }
   }
 }
 
@@ -183,87 +202,34 @@ struct ConvTrArgs {
 };
 constexpr int kTrMaxHits = 4;  // kernel <= 4 strides: taps landing on one output
 
-// Output s of channel o: (bias for complete outputs, else 0) + previous partial[s] (s <
-// overlap) + the taps tap = s % stride + h stride from step s / stride - h, in tap order (the
-// overlap_add of nn/kernels/conv.rs:117-166). A tap is sum_c w[c][o][tap] x[c][step] (one
-// sequential FMA chain), or w[o][tap] x[o][step] for a depthwise layer.
-template <int TS>
-__global__ void __launch_bounds__(kConvThreads) convtr1d_kernel(const ConvTrArgs a, int cc_max, int nstep) {
-  constexpr int TO = kConvThreads * 4 / TS;
-  extern __shared__ float sm[];
-  const int b = blockIdx.z, o0 = blockIdx.y * TO, s0 = blockIdx.x * TS;
-  const int tid = threadIdx.x, ol = tid % TO, g = tid / TO, o = o0 + ol;
+// Output s of channel o (s < t * stride + overlap): (bias for complete outputs, else 0) +
+// previous partial[s] (s < overlap) + the taps tap = s % stride + h stride from step
+// s / stride - h, in tap order (the overlap_add of nn/kernels/conv.rs:117-166). A tap's value
+// is prod[o * k + tap][step]: for an ungrouped layer the products were computed beforehand as
+// one 1x1 convolution (each a single FMA chain over the input channels); for a depthwise one
+// it is w[o][tap] x[o][step].
+__global__ void convtr_add_kernel(const ConvTrArgs a, const float* prod, int nb) {
   const int complete = a.t * a.stride, total = complete + a.overlap;
-  // Steps this tile reads: s / stride - h for s in [s0, s0 + TS), h <= (k - 1) / stride, so
-  // from s0 / stride - (k - 1) / stride (at least 0) to (s0 + TS - 1) / stride: at most nstep.
-  const int st0 = max(0, s0 / a.stride - (a.k - 1) / a.stride);
-  float acc[4][kTrMaxHits];
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)nb * a.cout * total) return;
+  const int s = (int)(i % total), o = (int)((i / total) % a.cout), b = (int)(i / ((int64_t)total * a.cout));
+  float v = s < complete && a.bias ? a.bias[o] : 0.f;
+  if (s < a.overlap) v = __fadd_rn(v, a.partial[((int64_t)(a.b0 + b) * a.cout + o) * a.overlap + s]);
 #pragma unroll
-  for (int i = 0; i < 4; i++)
-#pragma unroll
-    for (int h = 0; h < kTrMaxHits; h++) acc[i][h] = 0.f;
-  if (a.depthwise) {
-    if (o < a.cout)
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int s = s0 + 4 * g + i;
-#pragma unroll
-        for (int h = 0; h < kTrMaxHits; h++) {
-          const int tap = s % a.stride + h * a.stride, step = s / a.stride - h;
-          if (tap < a.k && step >= 0 && step < a.t) {
-            float xv = a.x[b * a.x_bs + (int64_t)o * a.x_cs + step];
-            if (a.act == ACT_ELU) xv = elu_ref(xv);
-            acc[i][h] = __fmul_rn(a.w[(int64_t)o * a.k + tap], xv);
-          }
-        }
-      }
-  } else {
-    const int tk = TO * a.k;
-    float* ws = sm;                  // [cc_max][TO * k]
-    float* xsm = sm + cc_max * tk;   // [cc_max][nstep]
-    for (int c0 = 0; c0 < a.cin; c0 += cc_max) {
-      const int cc = min(cc_max, a.cin - c0);
-      __syncthreads();
-      for (int i = tid; i < cc * tk; i += kConvThreads) {
-        const int c = i / tk, r = i - c * tk, oo = r / a.k;
-        ws[c * tk + r] = o0 + oo < a.cout ? a.w[((int64_t)(c0 + c) * a.cout + o0) * a.k + r] : 0.f;
-      }
-      for (int i = tid; i < cc * nstep; i += kConvThreads) {
-        const int c = i / nstep, u = i - c * nstep, step = st0 + u;
-        float xv = step < a.t ? a.x[b * a.x_bs + (int64_t)(c0 + c) * a.x_cs + step] : 0.f;
-        if (a.act == ACT_ELU && step < a.t) xv = elu_ref(xv);
-        xsm[c * nstep + u] = xv;
-      }
-      __syncthreads();
-      for (int c = 0; c < cc; c++) {
-        const float* wr = ws + c * tk + ol * a.k;
-        const float* xr = xsm + c * nstep;
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int s = s0 + 4 * g + i;
-#pragma unroll
-          for (int h = 0; h < kTrMaxHits; h++) {
-            const int tap = s % a.stride + h * a.stride, step = s / a.stride - h;
-            if (tap < a.k && step >= 0 && step < a.t) acc[i][h] = fmaf(wr[tap], xr[step - st0], acc[i][h]);
-          }
-        }
-      }
+  for (int h = 0; h < kTrMaxHits; h++) {
+    const int tap = s % a.stride + h * a.stride, step = s / a.stride - h;
+    if (tap >= a.k || step < 0 || step >= a.t) continue;
+    float p;
+    if (a.depthwise) {
+      float xv = a.x[b * a.x_bs + (int64_t)o * a.x_cs + step];
+      if (a.act == ACT_ELU) xv = elu_ref(xv);
+      p = __fmul_rn(a.w[(int64_t)o * a.k + tap], xv);
+    } else {
+      p = prod[(((int64_t)b * a.cout + o) * a.k + tap) * a.t + step];
     }
+    v = __fadd_rn(v, p);
   }
-  if (o >= a.cout) return;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int s = s0 + 4 * g + i;
-    if (s >= total) continue;
-    float v = s < complete && a.bias ? a.bias[o] : 0.f;
-    if (s < a.overlap) v = __fadd_rn(v, a.partial[((int64_t)(a.b0 + b) * a.cout + o) * a.overlap + s]);
-#pragma unroll
-    for (int h = 0; h < kTrMaxHits; h++) {
-      const int tap = s % a.stride + h * a.stride, step = s / a.stride - h;
-      if (tap < a.k && step >= 0 && step < a.t) v = __fadd_rn(v, acc[i][h]);
-    }
-    a.out[b * a.o_bs + (int64_t)o * a.o_cs + s] = v;
-  }
+  a.out[b * a.o_bs + (int64_t)o * a.o_cs + s] = v;
 }
 
 // The new partial: the tail outputs [t * stride, t * stride + overlap) of the chunk.
@@ -469,7 +435,7 @@ struct ConvLayer {
 
 // A step of a SEANet / codec pipeline: layer `layer` reads buffer `in` and writes `out` (both
 // channel-first; buffer ids below), with ELU on its input and an optional resnet skip.
-enum Buf { BUF_IN = 0, BUF_A = 1, BUF_B = 2, BUF_H = 3, BUF_OUT = 4, BUF_T = 5 };
+enum Buf { BUF_IN = 0, BUF_A = 1, BUF_B = 2, BUF_H = 3, BUF_OUT = 4, BUF_T = 5, BUF_P = 6 };
 struct ConvStep {
   int layer, in, out, act, skip;  // skip: a buffer id or -1
 };
@@ -499,8 +465,8 @@ struct CodecState {
   int max_batch = 0, max_frames = 0;
   DevBuf conv_state;           // [layer block][stream][...]
   DevBuf enc_started, dec_started;
-  DevBuf buf[4];               // A, B, H and the transformer's rows (ids 1..3, then rows)
-  int64_t buf_floats[4] = {0, 0, 0, 0};
+  DevBuf buf[5];               // blocks A, B, H, T and the transposed convolutions' products P
+  int64_t buf_floats[5] = {0, 0, 0, 0, 0};
   State* enc_ts = nullptr;
   State* dec_ts = nullptr;
   ~CodecState() {
@@ -556,7 +522,12 @@ struct CodecLoader {
     L.dil = dil;
     L.replicate = replicate;
     L.ctx = std::max(0, (k - 1) * dil + 1 - stride);  // StreamingConv1d::context
-    upload(L.w, need_tensor(t, n, prefix + ".weight", (int64_t)cout * cin * k).data, (int64_t)cout * cin * k, c.stream);
+    // Stored transposed, [cin * k][cout] (row c * k + j), for the kernel's coalesced staging.
+    const float* src = need_tensor(t, n, prefix + ".weight", (int64_t)cout * cin * k).data;
+    std::vector<float> tr((size_t)cout * cin * k);
+    for (int o = 0; o < cout; o++)
+      for (int r = 0; r < cin * k; r++) tr[(size_t)r * cout + o] = src[(size_t)o * cin * k + r];
+    upload(L.w, tr.data(), (int64_t)tr.size(), c.stream);
     if (bias) upload(L.bias, need_tensor(t, n, prefix + ".bias", cout).data, cout, c.stream);
     c.layers.push_back(std::move(L));
     return (int)c.layers.size() - 1;
@@ -753,38 +724,22 @@ struct View {
   int64_t bs() const { return (int64_t)C * rowlen; }
 };
 
-int odd_row(int words) { return words % 2 ? words : words + 1; }
-
 void launch_conv(const ConvArgs& a, int nb, cudaStream_t st) {
-  const bool narrow = a.len <= 8;
-  const int TL = narrow ? 4 : 32, TO = kConvThreads * 4 / TL;
-  const int xs = (TL - 1) * a.stride + (a.k - 1) * a.dil + 1;
-  int cc = std::min(a.cin, 64);
-  while (cc > 1 && ((int64_t)TO * odd_row(cc * a.k) + (int64_t)cc * xs) * 4 > kConvSmem) cc--;
-  const size_t smem = ((size_t)TO * odd_row(cc * a.k) + (size_t)cc * xs) * 4;
+  // Input channels per stage: both operands' rows, 2 x 64 floats per (channel, tap).
+  const int per_channel = 2 * kConvTile * a.k * 4;
+  const int cc = std::max(1, std::min(a.cin, kConvSmem / per_channel));
+  const size_t smem = (size_t)cc * per_channel;
   if (smem > (size_t)kConvSmem) throw Error(SVL_ERR_UNSUPPORTED, "convolution kernel too wide for one tile");
-  const dim3 grid((a.len + TL - 1) / TL, (a.cout + TO - 1) / TO, nb);
-  if (narrow)
-    conv1d_kernel<4><<<grid, kConvThreads, smem, st>>>(a, cc, odd_row(cc * a.k), xs);
-  else
-    conv1d_kernel<32><<<grid, kConvThreads, smem, st>>>(a, cc, odd_row(cc * a.k), xs);
+  const int64_t ncol = (int64_t)nb * a.len;
+  const dim3 grid((unsigned)((ncol + kConvTile - 1) / kConvTile), (a.cout + kConvTile - 1) / kConvTile);
+  conv1d_kernel<<<grid, kConvThreads, smem, st>>>(a, cc, nb);
   if (a.ctx > 0) conv_state_kernel<<<(nb * a.cin + 255) / 256, 256, 0, st>>>(a, nb);
 }
 
-void launch_convtr(const ConvTrArgs& a, int nb, cudaStream_t st) {
-  const int total = a.t * a.stride + a.overlap;
-  const bool narrow = total <= 8;
-  const int TS = narrow ? 4 : 32, TO = kConvThreads * 4 / TS;
-  const int nstep = (TS - 1) / a.stride + (a.k - 1) / a.stride + 2;
-  int cc = std::min(a.cin, 64);
-  while (cc > 1 && ((int64_t)cc * TO * a.k + (int64_t)cc * nstep) * 4 > kConvSmem) cc--;
-  const size_t smem = a.depthwise ? 0 : ((size_t)cc * TO * a.k + (size_t)cc * nstep) * 4;
-  if (smem > (size_t)kConvSmem) throw Error(SVL_ERR_UNSUPPORTED, "transposed convolution too wide for one tile");
-  const dim3 grid((total + TS - 1) / TS, (a.cout + TO - 1) / TO, nb);
-  if (narrow)
-    convtr1d_kernel<4><<<grid, kConvThreads, smem, st>>>(a, cc, nstep);
-  else
-    convtr1d_kernel<32><<<grid, kConvThreads, smem, st>>>(a, cc, nstep);
+// prod: for an ungrouped layer, the products [b][cout * k][t] (computed by the caller).
+void launch_convtr(const ConvTrArgs& a, const float* prod, int nb, cudaStream_t st) {
+  const int64_t n = (int64_t)nb * a.cout * (a.t * a.stride + a.overlap);
+  convtr_add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a, prod, nb);
   if (a.overlap > 0) convtr_state_kernel<<<(nb * a.cout * a.overlap + 255) / 256, 256, 0, st>>>(a, nb);
 }
 
@@ -794,12 +749,12 @@ struct Exec {
   CodecState& S;
   int nb;
   bool dry;
-  int64_t need[4] = {0, 0, 0, 0};
+  int64_t need[5] = {0, 0, 0, 0, 0};
   cudaStream_t st;
   const int* started;
 
   float* buf(int id, int64_t floats) {
-    const int i = id == BUF_A ? 0 : id == BUF_B ? 1 : id == BUF_H ? 2 : 3;  // BUF_T: 3
+    const int i = id == BUF_A ? 0 : id == BUF_B ? 1 : id == BUF_H ? 2 : id == BUF_P ? 4 : 3;  // BUF_T: 3
     need[i] = std::max(need[i], floats);
     if (dry) return nullptr;
     if (floats > S.buf_floats[i]) throw Error(SVL_ERR_INVALID_INPUT, "codec call larger than the state's max_frames");
@@ -830,8 +785,30 @@ struct Exec {
     } else {
       out.p = outp ? outp : buf(out_id, out.bs() * nb);
     }
+    // A transposed convolution's taps: products [b][cout * k][t] in block P.
+    float* prod = L.tr && !L.depthwise ? buf(BUF_P, (int64_t)L.cout * L.k * in.t * nb) : nullptr;
     if (dry) return out;
     if (L.tr) {
+      if (!L.depthwise) {
+        // The taps' products as a 1x1 convolution with cout * k output channels: the layer's
+        // weight [cin][cout][k] is that convolution's transposed weight [cin][cout * k].
+        ConvArgs p{};
+        p.x = in.p;
+        p.x_bs = in.bs();
+        p.x_cs = in.rowlen;
+        p.t = in.t;
+        p.started = started;
+        p.cin = L.cin;
+        p.cout = L.cout * L.k;
+        p.k = p.stride = p.dil = 1;
+        p.act = act;
+        p.w = L.w.as<float>();
+        p.out = prod;
+        p.o_bs = (int64_t)p.cout * in.t;
+        p.o_cs = in.t;
+        p.len = in.t;
+        launch_conv(p, nb, st);
+      }
       ConvTrArgs a{};
       a.x = in.p;
       a.x_bs = in.bs();
@@ -851,7 +828,7 @@ struct Exec {
       a.out = out.p;
       a.o_bs = out.bs();
       a.o_cs = out.rowlen;
-      launch_convtr(a, nb, st);
+      launch_convtr(a, prod, nb, st);
     } else {
       ConvArgs a{};
       a.x = in.p;
@@ -968,16 +945,16 @@ CodecState* create_codec_state(Codec* c, int max_batch, int max_frames) {
     S->max_batch = max_batch;
     S->max_frames = max_frames;
     // Size the work blocks by a dry run of the largest call of each half.
-    int64_t need[4] = {0, 0, 0, 0};
+    int64_t need[5] = {0, 0, 0, 0, 0};
     for (int half = 0; half < 2; half++) {
       if (half == 0 && !c->enc_tr) continue;
       if (half == 1 && !c->dec_tr) continue;
-      Exec E{*S, max_batch, true, {0, 0, 0, 0}, c->stream, nullptr};
+      Exec E{*S, max_batch, true, {0, 0, 0, 0, 0}, c->stream, nullptr};
       if (half == 0) encode(E, max_frames, nullptr, nullptr);
       else decode(E, max_frames, nullptr, nullptr);
-      for (int i = 0; i < 4; i++) need[i] = std::max(need[i], E.need[i]);
+      for (int i = 0; i < 5; i++) need[i] = std::max(need[i], E.need[i]);
     }
-    for (int i = 0; i < 4; i++) {
+    for (int i = 0; i < 5; i++) {
       S->buf_floats[i] = need[i];
       if (need[i] > 0) S->buf[i].alloc(need[i] * 4);
     }
@@ -1185,7 +1162,7 @@ SVL_API svl_status svl_mimi_encode_step_device(svl_mimi* mimi, svl_mimi_state* s
     if (frames < 1 || frames > S.max_frames) throw Error(SVL_ERR_INVALID_INPUT, "frames must be 1..max_frames");
     svl::check_cuda(cudaSetDevice(mimi->c->device), "cudaSetDevice");
     cudaStream_t st = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : mimi->c->stream;
-    svl::Exec E{S, batch, false, {0, 0, 0, 0}, st, S.enc_started.as<int>()};
+    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0}, st, S.enc_started.as<int>()};
     svl::encode(E, frames, d_pcm, d_latent);
     svl::mark_started_kernel<<<(batch + 255) / 256, 256, 0, st>>>(S.enc_started.as<int>(), batch);
     svl::check_cuda(cudaGetLastError(), "encode");
@@ -1203,7 +1180,7 @@ SVL_API svl_status svl_mimi_decode_step_device(svl_mimi* mimi, svl_mimi_state* s
     if (frames < 1 || frames > S.max_frames) throw Error(SVL_ERR_INVALID_INPUT, "frames must be 1..max_frames");
     svl::check_cuda(cudaSetDevice(mimi->c->device), "cudaSetDevice");
     cudaStream_t st = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : mimi->c->stream;
-    svl::Exec E{S, batch, false, {0, 0, 0, 0}, st, S.dec_started.as<int>()};
+    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0}, st, S.dec_started.as<int>()};
     svl::decode(E, frames, d_latent, d_pcm);
     svl::mark_started_kernel<<<(batch + 255) / 256, 256, 0, st>>>(S.dec_started.as<int>(), batch);
     svl::check_cuda(cudaGetLastError(), "decode");
