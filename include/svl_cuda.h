@@ -336,6 +336,19 @@ SVL_API svl_status svl_mimi_decode_step_device(svl_mimi* mimi, svl_mimi_state* s
                                                int32_t batch, int32_t frames,
                                                const float* d_latent, float* d_pcm,
                                                void* cuda_stream);
+/* Tts::decode_latent (tts/mod.rs:441-447) for streams 0..batch-1: d_latent
+ * [batch][frames][latent_dim] (FlowLm::step's output layout), times d_emb_std plus d_emb_mean
+ * ([latent_dim] each, the flow LM's "emb_std" / "emb_mean"; both NULL to skip), through the
+ * latent projection "quantizer.output_proj.weight" [outer_dim][latent_dim][1] (loaded by
+ * svl_mimi_create when present), then MimiDecoder::decode_step into d_pcm
+ * [batch][channels][frames * frame_size]. Device buffers on cuda_stream. */
+SVL_API svl_status svl_mimi_decode_latent_device(svl_mimi* mimi, svl_mimi_state* state,
+                                                 int32_t batch, int32_t frames,
+                                                 const float* d_latent, const float* d_emb_std,
+                                                 const float* d_emb_mean, float* d_pcm,
+                                                 void* cuda_stream);
+/* The latent width of the loaded latent projection (0 without one). */
+SVL_API int32_t svl_mimi_latent_dim(const svl_mimi* mimi);
 /* Quantizer::new (stt/model.rs:92-98): n_q codebooks of `bins` entries from the tensors
  * "quantizer.rvq_first.input_proj.weight" [256][512][1],
  * "quantizer.rvq_first.vq.layers.0._codebook.{embedding_sum,cluster_usage}" and the same under

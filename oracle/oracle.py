@@ -81,6 +81,7 @@ def lib() -> ctypes.CDLL:
             "orc_mimi_state_free": (None, [P]),
             "orc_mimi_encode_step": (I, [P, P, FP, I, FP]),
             "orc_mimi_decode_step": (I, [P, P, FP, I, FP]),
+            "orc_mimi_decode_latent": (I, [P, P, FP, I, FP, FP, FP]),
             "orc_rvq_create": (P, [I, I, ctypes.POINTER(_Tensor), I]),
             "orc_rvq_free": (None, [P]),
             "orc_rvq_encode": (I, [P, FP, I, UP]),
@@ -289,6 +290,23 @@ class OracleMimi:
         if lib().orc_mimi_decode_step(self.handle, state.handle, fp(latent), frames, fp(out)):
             raise ValueError("oracle decode failed")
         return out
+
+
+def _decode_latent(self, latent: np.ndarray, state, emb_std=None, emb_mean=None) -> np.ndarray:
+    """Tts::decode_latent: latent [frames][latent_dim] -> pcm [channels][frames * frame_size]."""
+    latent = np.ascontiguousarray(latent, np.float32)
+    frames = latent.shape[0]
+    out = np.zeros((self.cfg.decoder.channels, frames * self.frame_size), np.float32)
+    sd = None if emb_std is None else np.ascontiguousarray(emb_std, np.float32)
+    mn = None if emb_mean is None else np.ascontiguousarray(emb_mean, np.float32)
+    if lib().orc_mimi_decode_latent(self.handle, state.handle, fp(latent), frames,
+                                    fp(sd) if sd is not None else None,
+                                    fp(mn) if mn is not None else None, fp(out)):
+        raise ValueError("oracle decode_latent failed (no quantizer.output_proj.weight?)")
+    return out
+
+
+OracleMimi.decode_latent = _decode_latent
 
 
 class _MimiState:

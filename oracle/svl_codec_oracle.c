@@ -131,6 +131,7 @@ struct orc_mimi {
   ostep *enc, *dec;
   int n_enc, n_dec;
   int down, up, enc_in, enc_out, dec_in, dec_out;
+  int latent_proj, latent_dim; /* Tts::decode_latent's quantizer.output_proj (tts/mod.rs:218-224) */
   orc_lm *enc_tr, *dec_tr;
   float* owned_w[64];
   int n_owned;
@@ -251,7 +252,7 @@ static orc_tcfg tr_cfg(const orc_ptrans_cfg* p, int exact) {
 orc_mimi* orc_mimi_create(const orc_mimi_cfg* cfg, const orc_tensor* t, int n) {
   orc_mimi* m = (orc_mimi*)calloc(1, sizeof(orc_mimi));
   m->cfg = *cfg;
-  m->down = m->up = m->enc_in = m->enc_out = m->dec_in = m->dec_out = -1;
+  m->down = m->up = m->enc_in = m->enc_out = m->dec_in = m->dec_out = m->latent_proj = -1;
   m->frame_size = (int)lround((double)cfg->sample_rate / cfg->frame_rate);
   int ok = 1;
   char nm[256];
@@ -306,6 +307,11 @@ orc_mimi* orc_mimi_create(const orc_mimi_cfg* cfg, const orc_tensor* t, int n) {
     orc_tcfg tc = tr_cfg(p, cfg->exact_gelu);
     m->dec_tr = orc_transformer_create(&tc, "decoder_transformer.transformer.", t, n);
     if (!m->dec_tr) ok = 0;
+    const orc_tensor* lp = cfind(t, n, "quantizer.output_proj.weight");
+    if (lp && lp->numel > 0 && lp->numel % cfg->outer_dim == 0) {
+      m->latent_dim = (int)(lp->numel / cfg->outer_dim);
+      m->latent_proj = add_conv(m, t, n, "quantizer.output_proj", m->latent_dim, cfg->outer_dim, 1, 1, 1, 0, 0, &ok);
+    }
     int mult = 1 << s->n_ratios, li = 0, cur = OB_A;
     snprintf(nm, sizeof nm, "decoder.model.%d.conv", li++);
     int c0 = add_conv(m, t, n, nm, s->dimension, mult * s->n_filters, s->kernel_size, 1, 1, s->pad_mode, 1, &ok);
@@ -480,6 +486,28 @@ int orc_mimi_decode_step(orc_mimi* m, orc_mimi_state* S, const float* latent, in
   free(x.p);
   S->dec_started = 1;
   return 0;
+}
+
+/* Tts::decode_latent (tts/mod.rs:441-447): latent [frames][latent_dim] times emb_std plus
+ * emb_mean (both NULL: as is), the latent projection, then MimiDecoder::decode_step. */
+int orc_mimi_decode_latent(orc_mimi* m, orc_mimi_state* S, const float* latent, int frames,
+                           const float* emb_std, const float* emb_mean, float* pcm) {
+  if (m->latent_proj < 0 || frames <= 0) return -1;
+  const oconv* L = &m->convs[m->latent_proj];
+  float* x = (float*)malloc(sizeof(float) * (size_t)L->cin * frames);
+  for (int c = 0; c < L->cin; c++)
+    for (int f = 0; f < frames; f++) {
+      float v = latent[(size_t)f * L->cin + c];
+      if (emb_std) v = v * emb_std[c] + emb_mean[c];
+      x[(size_t)c * frames + f] = v;
+    }
+  oview in = {x, L->cin, frames};
+  int started = 1;
+  oview y = run_layer(S, m->latent_proj, in, 0, NULL, &started);
+  int rc = orc_mimi_decode_step(m, S, y.p, frames, pcm);
+  free(y.p);
+  free(x);
+  return rc;
 }
 
 /* ------------------------------------------------------------------ residual vector quantizer */

@@ -164,6 +164,11 @@ int orc_mimi_encode_step(orc_mimi*, orc_mimi_state*, const float* pcm, int frame
 /* latent [outer_dim][frames] -> pcm [channels][frames * frame_size]. */
 int orc_mimi_decode_step(orc_mimi*, orc_mimi_state*, const float* latent, int frames, float* pcm);
 
+/* Tts::decode_latent (tts/mod.rs:441-447): latent [frames][latent_dim], emb_std / emb_mean
+ * [latent_dim] (both NULL to skip), through "quantizer.output_proj.weight", then decode_step. */
+int orc_mimi_decode_latent(orc_mimi*, orc_mimi_state*, const float* latent, int frames,
+                           const float* emb_std, const float* emb_mean, float* pcm);
+
 /* Quantizer (stt/model.rs:84-170): latent [512][frames] -> codes [frames][n_q]. */
 orc_rvq* orc_rvq_create(int n_q, int bins, const orc_tensor* tensors, int n_tensors);
 void orc_rvq_free(orc_rvq*);

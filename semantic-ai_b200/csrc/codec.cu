@@ -35,7 +35,7 @@
 namespace svl {
 namespace {
 
-constexpr int ACT_NONE = 0, ACT_ELU = 1;
+constexpr int ACT_NONE = 0, ACT_ELU = 1, ACT_AFFINE = 2;  // ACT_AFFINE: x * scale[c] + shift[c]
 constexpr int kConvThreads = 256;
 constexpr int kConvSmem = 46 * 1024;  // under the 48 KB default: no opt-in needed
 
@@ -74,9 +74,11 @@ __device__ __forceinline__ float elu_ref(float x) {
 
 // One StreamingConv1d::forward over `nb` streams (streams b0 .. b0 + nb - 1 of the state).
 struct ConvArgs {
-  const float* x;  // input chunk [b][cin][t]: stream stride x_bs, channel stride x_cs
+  const float* x;  // input chunk [b][cin][t]: stream stride x_bs, channel stride x_cs, time stride x_ts
   int64_t x_bs;
-  int x_cs, t;
+  int x_cs, x_ts, t;
+  const float* in_scale;  // ACT_AFFINE: per input channel
+  const float* in_shift;
   float* prev;  // state [stream][cin][ctx]
   const int* started;  // [stream]: 0 before the stream's first chunk
   int b0, ctx;
@@ -90,15 +92,16 @@ struct ConvArgs {
 };
 
 // Value i of the convolution's input [previous context | act(chunk)] for stream b, channel c.
+__device__ __forceinline__ float conv_act(const ConvArgs& a, int c, float v) {
+  if (a.act == ACT_ELU) return elu_ref(v);
+  if (a.act == ACT_AFFINE) return __fadd_rn(__fmul_rn(v, a.in_scale[c]), a.in_shift[c]);
+  return v;
+}
 __device__ __forceinline__ float conv_in(const ConvArgs& a, int b, int c, int i, bool started) {
-  if (i >= a.ctx) {
-    const float v = a.x[b * a.x_bs + (int64_t)c * a.x_cs + (i - a.ctx)];
-    return a.act == ACT_ELU ? elu_ref(v) : v;
-  }
+  if (i >= a.ctx) return conv_act(a, c, a.x[b * a.x_bs + (int64_t)c * a.x_cs + (int64_t)(i - a.ctx) * a.x_ts]);
   if (started) return a.prev[((int64_t)(a.b0 + b) * a.cin + c) * a.ctx + i];
   if (!a.replicate) return 0.f;  // PadMode::Constant: zeros before the first chunk
-  const float v = a.x[b * a.x_bs + (int64_t)c * a.x_cs];  // PadMode::Replicate: the first sample
-  return a.act == ACT_ELU ? elu_ref(v) : v;
+  return conv_act(a, c, a.x[b * a.x_bs + (int64_t)c * a.x_cs]);  // PadMode::Replicate: the first sample
 }
 
 // CTA tile: 64 output channels x 64 columns, a column being one output time of one stream
@@ -435,7 +438,7 @@ struct ConvLayer {
 
 // A step of a SEANet / codec pipeline: layer `layer` reads buffer `in` and writes `out` (both
 // channel-first; buffer ids below), with ELU on its input and an optional resnet skip.
-enum Buf { BUF_IN = 0, BUF_A = 1, BUF_B = 2, BUF_H = 3, BUF_OUT = 4, BUF_T = 5, BUF_P = 6 };
+enum Buf { BUF_IN = 0, BUF_A = 1, BUF_B = 2, BUF_H = 3, BUF_OUT = 4, BUF_T = 5, BUF_P = 6, BUF_L = 7 };
 struct ConvStep {
   int layer, in, out, act, skip;  // skip: a buffer id or -1
 };
@@ -449,6 +452,7 @@ struct Codec {
   std::vector<ConvStep> enc_seanet, dec_seanet;
   int down = -1, up = -1;
   int enc_in_proj = -1, enc_out_proj = -1, dec_in_proj = -1, dec_out_proj = -1;
+  int latent_proj = -1, latent_dim = 0;  // Pocket TTS's quantizer.output_proj (tts/mod.rs:218-224)
   Model* enc_tr = nullptr;
   Model* dec_tr = nullptr;
   int64_t state_floats = 0;  // per stream
@@ -465,8 +469,8 @@ struct CodecState {
   int max_batch = 0, max_frames = 0;
   DevBuf conv_state;           // [layer block][stream][...]
   DevBuf enc_started, dec_started;
-  DevBuf buf[5];               // blocks A, B, H, T and the transposed convolutions' products P
-  int64_t buf_floats[5] = {0, 0, 0, 0, 0};
+  DevBuf buf[6];  // blocks A, B, H, T, the transposed convolutions' products P, projected latents L
+  int64_t buf_floats[6] = {0, 0, 0, 0, 0, 0};
   State* enc_ts = nullptr;
   State* dec_ts = nullptr;
   ~CodecState() {
@@ -686,6 +690,15 @@ Codec* create_codec(const svl_mimi_config& cfg, const svl_tensor_view* t, int n,
       if (p.output_dimension != s.dimension) throw Error(SVL_ERR_CONFIG, "decoder transformer output width != SEANet dimension");
       const svl_transformer_config tc = projected_cfg(p, cfg.exact_gelu);
       c->dec_tr = create_model(2, tc, nullptr, nullptr, t, n, device, "decoder_transformer.transformer.");
+      // The latent projection of Tts::decode_latent (tts/mod.rs:218-224, :441-447), when the
+      // tensors carry it: "quantizer.output_proj.weight" [outer_dim][latent_dim][1].
+      for (int i = 0; i < n; i++)
+        if (t[i].name && std::string(t[i].name) == "quantizer.output_proj.weight") {
+          if (t[i].numel <= 0 || t[i].numel % cfg.outer_dim)
+            throw Error(SVL_ERR_CONFIG, "quantizer.output_proj.weight is not [outer_dim][latent][1]");
+          c->latent_dim = (int)(t[i].numel / cfg.outer_dim);
+          c->latent_proj = ld.conv("quantizer.output_proj", c->latent_dim, cfg.outer_dim, 1, 1, 1, 0, false);
+        }
       // SeanetDecoder::new (nn/seanet.rs:197-235).
       auto name = [](int i) { return "decoder.model." + std::to_string(i); };
       int mult = 1 << s.n_ratios, li = 0, cur = BUF_A;
@@ -749,12 +762,12 @@ struct Exec {
   CodecState& S;
   int nb;
   bool dry;
-  int64_t need[5] = {0, 0, 0, 0, 0};
+  int64_t need[6] = {0, 0, 0, 0, 0, 0};
   cudaStream_t st;
   const int* started;
 
   float* buf(int id, int64_t floats) {
-    const int i = id == BUF_A ? 0 : id == BUF_B ? 1 : id == BUF_H ? 2 : id == BUF_P ? 4 : 3;  // BUF_T: 3
+    const int i = id == BUF_A ? 0 : id == BUF_B ? 1 : id == BUF_H ? 2 : id == BUF_P ? 4 : id == BUF_L ? 5 : 3;  // BUF_T: 3
     need[i] = std::max(need[i], floats);
     if (dry) return nullptr;
     if (floats > S.buf_floats[i]) throw Error(SVL_ERR_INVALID_INPUT, "codec call larger than the state's max_frames");
@@ -796,6 +809,7 @@ struct Exec {
         p.x = in.p;
         p.x_bs = in.bs();
         p.x_cs = in.rowlen;
+        p.x_ts = 1;
         p.t = in.t;
         p.started = started;
         p.cin = L.cin;
@@ -834,6 +848,7 @@ struct Exec {
       a.x = in.p;
       a.x_bs = in.bs();
       a.x_cs = in.rowlen;
+      a.x_ts = 1;
       a.t = in.t;
       a.prev = layer_state(L);
       a.started = started;
@@ -936,6 +951,39 @@ void decode(Exec& E, int frames, const float* latent, float* pcm) {
   E.seanet(c.dec_seanet, x, pcm);
 }
 
+// Tts::decode_latent (tts/mod.rs:441-447): latents [b][frames][latent_dim] (the flow LM's
+// layout), times emb_std plus emb_mean (null: left as they are), through the latent projection
+// into [b][outer_dim][frames], then MimiDecoder::decode_step.
+void decode_latent(Exec& E, int frames, const float* latent, const float* std_, const float* mean,
+                   float* pcm) {
+  Codec& c = *E.S.c;
+  const ConvLayer& L = c.layers[c.latent_proj];
+  float* proj = E.buf(BUF_L, (int64_t)L.cout * frames * E.nb);
+  if (!E.dry) {
+    ConvArgs a{};
+    a.x = latent;
+    a.x_bs = (int64_t)frames * L.cin;
+    a.x_cs = 1;
+    a.x_ts = L.cin;
+    a.t = frames;
+    a.act = std_ ? ACT_AFFINE : ACT_NONE;
+    a.in_scale = std_;
+    a.in_shift = mean;
+    a.started = E.started;
+    a.cin = L.cin;
+    a.cout = L.cout;
+    a.k = a.stride = a.dil = 1;
+    a.w = L.w.as<float>();
+    a.out = proj;
+    a.o_bs = (int64_t)L.cout * frames;
+    a.o_cs = frames;
+    a.len = frames;
+    launch_conv(a, E.nb, E.st);
+    check_cuda(cudaGetLastError(), "latent projection launch");
+  }
+  decode(E, frames, proj, pcm);
+}
+
 CodecState* create_codec_state(Codec* c, int max_batch, int max_frames) {
   if (max_batch <= 0 || max_frames <= 0) throw Error(SVL_ERR_INVALID_INPUT, "max_batch and max_frames must be positive");
   check_cuda(cudaSetDevice(c->device), "cudaSetDevice");
@@ -945,16 +993,17 @@ CodecState* create_codec_state(Codec* c, int max_batch, int max_frames) {
     S->max_batch = max_batch;
     S->max_frames = max_frames;
     // Size the work blocks by a dry run of the largest call of each half.
-    int64_t need[5] = {0, 0, 0, 0, 0};
+    int64_t need[6] = {0, 0, 0, 0, 0, 0};
     for (int half = 0; half < 2; half++) {
       if (half == 0 && !c->enc_tr) continue;
       if (half == 1 && !c->dec_tr) continue;
-      Exec E{*S, max_batch, true, {0, 0, 0, 0, 0}, c->stream, nullptr};
+      Exec E{*S, max_batch, true, {0, 0, 0, 0, 0, 0}, c->stream, nullptr};
       if (half == 0) encode(E, max_frames, nullptr, nullptr);
+      else if (c->latent_proj >= 0) decode_latent(E, max_frames, nullptr, nullptr, nullptr, nullptr);
       else decode(E, max_frames, nullptr, nullptr);
-      for (int i = 0; i < 5; i++) need[i] = std::max(need[i], E.need[i]);
+      for (int i = 0; i < 6; i++) need[i] = std::max(need[i], E.need[i]);
     }
-    for (int i = 0; i < 5; i++) {
+    for (int i = 0; i < 6; i++) {
       S->buf_floats[i] = need[i];
       if (need[i] > 0) S->buf[i].alloc(need[i] * 4);
     }
@@ -1162,7 +1211,7 @@ SVL_API svl_status svl_mimi_encode_step_device(svl_mimi* mimi, svl_mimi_state* s
     if (frames < 1 || frames > S.max_frames) throw Error(SVL_ERR_INVALID_INPUT, "frames must be 1..max_frames");
     svl::check_cuda(cudaSetDevice(mimi->c->device), "cudaSetDevice");
     cudaStream_t st = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : mimi->c->stream;
-    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0}, st, S.enc_started.as<int>()};
+    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0, 0}, st, S.enc_started.as<int>()};
     svl::encode(E, frames, d_pcm, d_latent);
     svl::mark_started_kernel<<<(batch + 255) / 256, 256, 0, st>>>(S.enc_started.as<int>(), batch);
     svl::check_cuda(cudaGetLastError(), "encode");
@@ -1180,12 +1229,36 @@ SVL_API svl_status svl_mimi_decode_step_device(svl_mimi* mimi, svl_mimi_state* s
     if (frames < 1 || frames > S.max_frames) throw Error(SVL_ERR_INVALID_INPUT, "frames must be 1..max_frames");
     svl::check_cuda(cudaSetDevice(mimi->c->device), "cudaSetDevice");
     cudaStream_t st = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : mimi->c->stream;
-    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0}, st, S.dec_started.as<int>()};
+    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0, 0}, st, S.dec_started.as<int>()};
     svl::decode(E, frames, d_latent, d_pcm);
     svl::mark_started_kernel<<<(batch + 255) / 256, 256, 0, st>>>(S.dec_started.as<int>(), batch);
     svl::check_cuda(cudaGetLastError(), "decode");
   });
 }
+
+SVL_API svl_status svl_mimi_decode_latent_device(svl_mimi* mimi, svl_mimi_state* state, int32_t batch,
+                                                 int32_t frames, const float* d_latent, const float* d_emb_std,
+                                                 const float* d_emb_mean, float* d_pcm, void* cuda_stream) {
+  return svl::codec_guarded([&] {
+    if (!mimi || !state || !d_pcm || !d_latent) throw Error(SVL_ERR_INVALID_INPUT, "null argument");
+    if (!d_emb_std != !d_emb_mean) throw Error(SVL_ERR_INVALID_INPUT, "emb_std and emb_mean go together");
+    svl::CodecState& S = *state->s;
+    if (S.c != mimi->c) throw Error(SVL_ERR_INVALID_INPUT, "state of another codec");
+    if (!mimi->c->dec_tr) throw Error(SVL_ERR_INVALID_INPUT, "the codec was created without its decoder");
+    if (mimi->c->latent_proj < 0)
+      throw Error(SVL_ERR_INVALID_INPUT, "the codec was created without quantizer.output_proj.weight");
+    if (batch < 1 || batch > S.max_batch) throw Error(SVL_ERR_INVALID_INPUT, "batch out of range");
+    if (frames < 1 || frames > S.max_frames) throw Error(SVL_ERR_INVALID_INPUT, "frames must be 1..max_frames");
+    svl::check_cuda(cudaSetDevice(mimi->c->device), "cudaSetDevice");
+    cudaStream_t st = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : mimi->c->stream;
+    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0, 0}, st, S.dec_started.as<int>()};
+    svl::decode_latent(E, frames, d_latent, d_emb_std, d_emb_mean, d_pcm);
+    svl::mark_started_kernel<<<(batch + 255) / 256, 256, 0, st>>>(S.dec_started.as<int>(), batch);
+    svl::check_cuda(cudaGetLastError(), "decode");
+  });
+}
+
+SVL_API int32_t svl_mimi_latent_dim(const svl_mimi* mimi) { return mimi ? mimi->c->latent_dim : 0; }
 
 SVL_API svl_status svl_rvq_create(int32_t n_q, int32_t bins, const svl_tensor_view* tensors, int32_t n_tensors,
                                   int32_t device, svl_rvq** out) {

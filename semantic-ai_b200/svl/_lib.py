@@ -62,6 +62,8 @@ SIGNATURES = {
     "svl_mimi_state_reset": (_I, [_P, _I]),
     "svl_mimi_encode_step_device": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "svl_mimi_decode_step_device": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "svl_mimi_decode_latent_device": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
+    "svl_mimi_latent_dim": (_I, [_P]),
     "svl_rvq_create": (_I, [_I, _I, _P, _I, _I, ctypes.POINTER(_P)]),
     "svl_rvq_destroy": (None, [_P]),
     "svl_rvq_encode_device": (_I, [_P, _I, _I, _P, _P, _P]),

@@ -218,6 +218,19 @@ class Mimi:
               ctypes.c_void_p(latent.data_ptr()), ctypes.c_void_p(out.data_ptr()), stream=stream)
         return out
 
+    def decode_latent(self, latent, state: MimiState, emb_std=None, emb_mean=None, stream=None):
+        """Tts::decode_latent (tts/mod.rs:441-447): latent, CUDA float32 [batch][frames][latent_dim]
+        (FlowLm::step's layout), times emb_std plus emb_mean (CUDA [latent_dim], or None), through
+        quantizer.output_proj, then decode_step -> pcm [batch][channels][frames * frame_size]."""
+        import torch
+        b, frames, _ = latent.shape
+        out = torch.empty((b, self.cfg.decoder.channels, frames * self.frame_size),
+                          dtype=torch.float32, device=latent.device)
+        ptr = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+        _call(_lib.lib().svl_mimi_decode_latent_device, self.handle, state.handle, b, frames,
+              ptr(latent), ptr(emb_std), ptr(emb_mean), ptr(out), stream=stream)
+        return out
+
     def close(self):
         if self.handle:
             _lib.lib().svl_mimi_destroy(self.handle)

@@ -166,7 +166,7 @@ def _ptrans_spec(prefix: str, p):
     return out
 
 
-def mimi_specs(cfg):
+def mimi_specs(cfg, latent_dim: int | None = None):
     """Tensor names of MimiEncoder::new / MimiDecoder::new (nn/mimi.rs:140-166, :229-251) after
     load_mimi_weights' renaming (nn/mod.rs:26-52). Convolutions are N(0, 1 / fan_in) so that
     activations keep their scale through the SEANet stacks."""
@@ -195,6 +195,8 @@ def mimi_specs(cfg):
     if cfg.parts & DECODER:
         s = cfg.decoder
         st = cfg.resample_stride(s)
+        if latent_dim:  # Pocket TTS: the flow LM's latents into the decoder (tts/mod.rs:218-224)
+            out.append(("quantizer.output_proj.weight", (cfg.outer_dim, latent_dim, 1), ("fan", latent_dim)))
         if st > 1:
             out.append(("upsample.convtr.convtr.weight", (cfg.outer_dim, 1, 2 * st), ("fan", 2)))
         out += _ptrans_spec("decoder_transformer", cfg.decoder_transformer)
@@ -253,8 +255,8 @@ def materialize_codec(specs, seed: int = 0, std: float = 0.02) -> dict[str, np.n
     return out
 
 
-def mimi_weights(cfg, seed: int = 0):
-    return materialize_codec(mimi_specs(cfg), seed)
+def mimi_weights(cfg, seed: int = 0, latent_dim: int | None = None):
+    return materialize_codec(mimi_specs(cfg, latent_dim), seed)
 
 
 def rvq_weights(n_q: int, bins: int, seed: int = 0):
