@@ -12,7 +12,8 @@ batches ("weak" scaling, no collective on the data path).
 
 The default workload is BASELINE config 2 (STT-1b, q8_0 weights, batch 1), timed at a steady
 state (every frame attends to the full 750-key window); the same run then measures BASELINE
-config 3 (STT-1b bf16, 256 streams per GPU at staggered fills) under the key "config3".
+config 3 (STT-1b bf16, 256 streams per GPU at staggered fills) under the key "config3", and the
+Mimi codec (encoder + quantizer, decoder; 64 streams per GPU) under the key "codec".
 --layers L builds the workload with its first L layers only: the small cases for ncu
 captures (such a line is a profiling case, not a benchmark number).
 """
@@ -376,6 +377,14 @@ def run_ours(args, spec, rank, world, local_rank):
                           "kernels": r3["kernels"], "clocks": r3["clocks"]}
         del m3
         gc.collect()
+    # The codec around the LMs in the same run: 64 streams per GPU, one
+    # frame per step, 50 timed steps.
+    if args.config == "2" and not args.no_codec and not args.layers:
+        sc = dict(CONFIGS["codec"], key="codec")
+        cd = measure_codec(args, sc, rank, world, local_rank, dist, 50, 5, cpu=False)
+        out["codec"] = {k: cd[k] for k in ("metric", "value", "unit", "ms_per_step", "dtype", "config",
+                                           "e2e", "roofline", "decoder")}
+        gc.collect()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(spec, stt, cfg, weights, budget_s=args.cpu_seconds)
     if dist:
@@ -584,6 +593,19 @@ def codec_flops(cfg, part) -> int:
 
 
 def run_codec(args, spec, rank, world, local_rank):
+    import torch
+    torch.cuda.set_device(local_rank)
+    dist = init_dist(world, local_rank)
+    out = measure_codec(args, spec, rank, world, local_rank, dist, args.steps, args.warmup,
+                        cpu=not args.no_cpu_baseline)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def measure_codec(args, spec, rank, world, local_rank, dist, K, W, cpu=True):
     """The codec on both sides of the LMs, one codec frame (80 ms) of every stream per step: the
     STT Mimi encoder followed by the quantizer (audio -> the LM's 32 audio tokens, stt/mod.rs:
     532-541), and the Pocket-TTS Mimi decoder (latents -> audio, tts/mod.rs:441-447). f32 on the
@@ -592,9 +614,7 @@ def run_codec(args, spec, rank, world, local_rank):
     import oracle
     from svl import codec
 
-    torch.cuda.set_device(local_rank)
-    dist = init_dist(world, local_rank)
-    B, K, W = spec["batch"], args.steps, args.warmup
+    B = spec["batch"]
     peaks, src = load_peaks()
     props = torch.cuda.get_device_properties(local_rank)
     fp32_peak = props.multi_processor_count * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
@@ -667,7 +687,7 @@ def run_codec(args, spec, rank, world, local_rank):
                             "frac": round(flops / (ms * 1e-3) / 1e12 / fp32_peak, 4),
                             "peak_source": "nominal FP32 FMA rate (SMs x 128 x 2 x max SM clock)",
                             "flops_per_step": flops}}
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if rank == 0 and world == 1 and cpu:
             om = oracle.OracleMimi(cfg, w)
             oq = oracle.OracleQuantizer(32, 2048, w) if part == codec.ENCODER else None
             os_ = om.init_state()
@@ -689,11 +709,7 @@ def run_codec(args, spec, rank, world, local_rank):
                decoder=legs["decoder"])
     if "cpu_baseline" in legs["encoder+rvq"]:
         out["cpu_baseline"] = legs["encoder+rvq"]["cpu_baseline"]
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(out), flush=True)
+    return out
 
 
 def cpu_baseline_tts(cfg, tts, weights, prompt, budget_s=15.0, frames_cap=None):
@@ -858,6 +874,8 @@ def main():
                     help="first L layers only: a small case for profiling captures")
     ap.add_argument("--no-config3", action="store_true",
                     help="skip the config-3 block of the default (config 2) run")
+    ap.add_argument("--no-codec", action="store_true",
+                    help="skip the codec block of the default (config 2) run")
     args = ap.parse_args()
     spec = dict(CONFIGS[args.config], key=args.config)
     if args.steps is None:
