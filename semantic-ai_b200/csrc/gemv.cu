@@ -620,6 +620,10 @@ int pick_r(const GemvParams& p) {
 // four-row groups.
 template <int WT, int R>
 constexpr int kU = WT == W_F32 ? 8 : R == 4 ? 2 : 4;
+// 16 streams per launch (f32 weights only, see max_nb): 4 loads per row in flight, so that
+// the weights in flight and the 16 streams' accumulators fit the registers.
+template <int WT, int NB, int R>
+constexpr int kUn = NB == 16 ? 4 : kU<WT, R>;
 // CTAs of a quantised product: one group at least each, at most kGrid.
 constexpr int kQGrid = kGrid;
 
@@ -646,7 +650,7 @@ template <int WT, int NB, int R>
 void launch_r(const GemvParams& p, cudaStream_t s) {
   const int groups = (p.n + R - 1) / R;
   const int grid = std::min((groups + kWarps - 1) / kWarps, kGrid);
-  launch_k(gemv_kernel<WT, NB, R, kU<WT, R>>, p, grid, (size_t)NB * rec_bytes(p), s);
+  launch_k(gemv_kernel<WT, NB, R, kUn<WT, NB, R>>, p, grid, (size_t)NB * rec_bytes(p), s);
 }
 
 // Four-row groups only where their registers fit without spilling (one stream, bf16).
@@ -718,11 +722,29 @@ void set_attrs() {
   set_attrs_nb<WT, 2>();
   set_attrs_nb<WT, 4>();
   set_attrs_nb<WT, 8>();
+  if constexpr (WT == W_F32) {
+    cudaFuncSetAttribute(gemv_kernel<WT, 16, 1, kUn<WT, 16, 1>>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    cudaFuncSetAttribute(gemv_kernel<WT, 16, 2, kUn<WT, 16, 2>>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  }
+}
+
+// 9 to 16 streams of an f32 product in one launch (max_nb decides when).
+void launch_t16(const GemvParams& p, cudaStream_t s) {
+  if (pick_r(p) == 1)
+    launch_r<W_F32, 16, 1>(p, s);
+  else
+    launch_r<W_F32, 16, 2>(p, s);
 }
 
 // Streams per launch: the widest template whose input records fit (with, for the quantised
-// kernel, at least one staged group of rows).
+// kernel, at least one staged group of rows). f32 weights with many streams (Mimi's
+// transformers, f32 models) take 16 per launch where the records fit, halving the passes over
+// the weights; not for the logits head (its argmax scratch holds 8 streams per launch) nor in
+// reference order.
 int max_nb(const GemvParams& p) {
+  if (p.wtype == W_F32 && p.nb > 8 && p.epi != EPI_LOGITS && !p.ref_order &&
+      (size_t)16 * rec_bytes(p) <= kMaxSmem)
+    return 16;
   const bool q = p.wtype == W_Q8 || p.wtype == W_Q4;
   for (int nb : {8, 4, 2}) {
     if (q ? kQHeader + q_records_area(p.wtype, p.k, nb) + 4 * (size_t)p.row_stride <= kQSmemBudget
@@ -750,6 +772,12 @@ void launch_w(const GemvParams& p0, cudaStream_t s) {
     }
     if (b0 > 0)
       for (auto& r : p.pf) r = PrefetchRange{};
+    if constexpr (WT == W_F32) {
+      if (p.nb > 8) {
+        launch_t16(p, s);
+        continue;
+      }
+    }
     switch (p.nb) {
       case 1: launch_t<WT, 1>(p, s); break;
       case 2: launch_t<WT, 2>(p, s); break;
