@@ -134,15 +134,28 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvArgs a, 
       const int r = i / T, o = i - r * T;
       ws[i] = o0 + o < a.cout ? a.w[((int64_t)c0 * a.k + r) * a.cout + o0 + o] : 0.f;
     }
+    // The gather: column-fastest walks one stream's time axis when a tile holds a single
+    // stream's outputs (long chunks); tap-fastest keeps a warp on contiguous samples of one
+    // stream's window when the tile's columns jump between streams (short chunks).
+    const bool tap_fast = a.len < T;
     for (int i = tid; i < ck * T; i += kConvThreads) {
-      const int r = i / T, col = i - r * T, q = q0 + col;
+      int r, col;
+      if (tap_fast) {
+        const int j = i % a.k, rest = i / a.k;
+        col = rest % T;
+        r = (rest / T) * a.k + j;
+      } else {
+        r = i / T;
+        col = i - r * T;
+      }
+      const int q = q0 + col;
       float v = 0.f;
       if (q < ncol) {
         const int b = q / a.len, l = q - b * a.len, c = r / a.k, j = r - c * a.k;
         const int pos = l * a.stride + j * a.dil;
         if (pos < total) v = conv_in(a, b, c0 + c, pos, a.started[a.b0 + b] != 0);
       }
-      xsm[i] = v;
+      xsm[r * T + col] = v;
     }
     __syncthreads();
     const float* wb = ws + 4 * og;
@@ -246,7 +259,8 @@ __global__ void convtr_state_kernel(const ConvTrArgs a, int nb) {
 
 // ---- split residual vector quantizer (Quantizer::encode, stt/model.rs:100-170) -------------
 //
-// A row is one latent frame of one stream. A cluster of kRvqRanks CTAs takes kRvqRows rows;
+// A row is one latent frame of one stream. A cluster of kRvqRanks CTAs takes R rows (8, or 4 / 2
+// for small batches);
 // CTA `rank` owns entries [rank * per, (rank + 1) * per) of every codebook. Each CTA keeps the
 // rows' latents and residuals in shared memory, so per codebook a thread scores its entries
 // against the residuals (dist = half_norm - entry . residual, Codebook::encode), the CTA finds
@@ -258,7 +272,7 @@ __global__ void convtr_state_kernel(const ConvTrArgs a, int nb) {
 // threads of a warp read consecutive entries.
 constexpr int kRvqDim = 256;   // ResidualQuantizer::DIM
 constexpr int kRvqIn = 512;    // the latent width Quantizer::new expects
-constexpr int kRvqRows = 8;
+constexpr int kRvqMaxRows = 8;  // rows per cluster: 8, or 4 / 2 for small batches (more CTAs)
 constexpr int kRvqRanks = 8;
 constexpr int kRvqThreads = 256;
 
@@ -280,8 +294,9 @@ __device__ __forceinline__ bool rvq_better(float v, int i, float bv, int bi) {
   return v < bv || (v == bv && i < bi);
 }
 
+template <int R>
 __global__ void __launch_bounds__(kRvqThreads) rvq_kernel(const RvqArgs a) {
-  constexpr int R = kRvqRows, NW = kRvqThreads / 32;
+  constexpr int NW = kRvqThreads / 32;
   __shared__ float xs[R][kRvqIn];
   __shared__ float res[R][kRvqDim];
   __shared__ float cand_v[2][kRvqRanks][R];
@@ -313,10 +328,15 @@ __global__ void __launch_bounds__(kRvqThreads) rvq_kernel(const RvqArgs a) {
       float acc[R];
 #pragma unroll
       for (int r = 0; r < R; r++) acc[r] = 0.f;
-      for (int c = 0; c < kRvqIn; c++) {
-        const float wv = pt[(int64_t)c * kRvqDim + tid];
+      // 16 weights in flight per thread, then their FMAs in order.
+      for (int c0 = 0; c0 < kRvqIn; c0 += 16) {
+        float wv[16];
 #pragma unroll
-        for (int r = 0; r < R; r++) acc[r] = fmaf(wv, xs[r][c], acc[r]);
+        for (int u = 0; u < 16; u++) wv[u] = pt[(int64_t)(c0 + u) * kRvqDim + tid];
+#pragma unroll
+        for (int u = 0; u < 16; u++)
+#pragma unroll
+          for (int r = 0; r < R; r++) acc[r] = fmaf(wv[u], xs[r][c0 + u], acc[r]);
       }
 #pragma unroll
       for (int r = 0; r < R; r++) res[r][tid] = acc[r];
@@ -335,10 +355,14 @@ __global__ void __launch_bounds__(kRvqThreads) rvq_kernel(const RvqArgs a) {
       float acc[R];
 #pragma unroll
       for (int r = 0; r < R; r++) acc[r] = 0.f;
-      for (int d = 0; d < kRvqDim; d++) {
-        const float e = et[(int64_t)d * a.bins + j];
+      for (int d0 = 0; d0 < kRvqDim; d0 += 16) {
+        float e[16];
 #pragma unroll
-        for (int r = 0; r < R; r++) acc[r] = fmaf(e, res[r][d], acc[r]);
+        for (int u = 0; u < 16; u++) e[u] = et[(int64_t)(d0 + u) * a.bins + j];
+#pragma unroll
+        for (int u = 0; u < 16; u++)
+#pragma unroll
+          for (int r = 0; r < R; r++) acc[r] = fmaf(e[u], res[r][d0 + u], acc[r]);
       }
       const float h = a.hn[(int64_t)q * a.bins + j];
 #pragma unroll
@@ -1104,8 +1128,11 @@ void rvq_encode(Rvq& q, int nb, int frames, const float* latent, uint32_t* codes
   a.n_q = q.n_q;
   a.bins = q.bins;
   a.codes = codes;
+  // Rows per cluster: enough clusters to cover the SMs (each CTA scores its entries for its
+  // cluster's rows; fewer rows per cluster means more CTAs reading the same codebook slices).
+  const int R = a.rows <= 32 ? 2 : a.rows <= 96 ? 4 : kRvqMaxRows;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kRvqRanks, (a.rows + kRvqRows - 1) / kRvqRows, 1);
+  cfg.gridDim = dim3(kRvqRanks, (a.rows + R - 1) / R, 1);
   cfg.blockDim = dim3(kRvqThreads);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1115,7 +1142,12 @@ void rvq_encode(Rvq& q, int nb, int frames, const float* latent, uint32_t* codes
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  check_cuda(cudaLaunchKernelEx(&cfg, rvq_kernel, a), "RVQ launch");
+  if (R == 2)
+    check_cuda(cudaLaunchKernelEx(&cfg, rvq_kernel<2>, a), "RVQ launch");
+  else if (R == 4)
+    check_cuda(cudaLaunchKernelEx(&cfg, rvq_kernel<4>, a), "RVQ launch");
+  else
+    check_cuda(cudaLaunchKernelEx(&cfg, rvq_kernel<kRvqMaxRows>, a), "RVQ launch");
 }
 
 template <class F>

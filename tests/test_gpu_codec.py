@@ -126,9 +126,11 @@ def test_mimi_rejects_bad_calls(svl_lib):
         codec.Mimi(cfg, w)
 
 
-@pytest.mark.parametrize("n_q,bins,streams,frames", [(32, 2048, 5, 3), (8, 300, 9, 1), (1, 64, 2, 2)])
+@pytest.mark.parametrize("n_q,bins,streams,frames",
+                         [(32, 2048, 5, 3), (8, 300, 9, 1), (1, 64, 2, 2), (32, 2048, 20, 3), (32, 2048, 40, 3)])
 def test_quantizer_bit_exact(svl_lib, n_q, bins, streams, frames):
-    """Quantizer::encode on the same latents: codes identical to the oracle's."""
+    """Quantizer::encode on the same latents: codes identical to the oracle's (rows per cluster:
+    2 for up to 32 rows, 4 up to 96, 8 above)."""
     import torch
     w = synth.rvq_weights(n_q, bins)
     gq, oq = codec.Quantizer(n_q, bins, w), oracle.OracleQuantizer(n_q, bins, w)
