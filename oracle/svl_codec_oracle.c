@@ -9,7 +9,8 @@
  * Follows, for one stream:
  *  - StreamingConv1d::forward (nn/conv.rs:122-179) with im2col (nn/kernels/conv.rs:8-85):
  *    the carried-over context, constant / replicate padding of the first chunk, output l =
- *    sum over (channel c, tap j) of w[o][c][j] x[l stride + j dil], then + bias;
+ *    sum over (channel c, tap j) of w[o][c][j] x[l stride + j dil], then + bias; the sum is
+ *    blocked in chunks of floor(1024 / k) channels (FMA chains, then the chunks' sums in order);
  *  - StreamingConvTranspose1d::forward_taps (nn/conv.rs:296-323) with overlap_add
  *    (nn/kernels/conv.rs:87-166): bias on the complete outputs, + the previous partial, + the
  *    taps in tap order; the tail becomes the next partial;
@@ -20,7 +21,7 @@
  *  - Quantizer / ResidualQuantizer / Codebook (stt/model.rs:84-170).
  *
  * Parity status: the products inside candle's matmul (gemm crate, blocked) have an order of
- * their own; this file sums each output as one sequential FMA chain in im2col column order, so
+ * their own; this file sums each output in fixed chunks of im2col columns (one FMA chain each), so
  * against candle the convolutions and distances are "parity unpinned" (tolerance-level), while
  * the streaming semantics (context, padding, overlap-add order, argmin ties) follow the source.
  * The reference's own tests for these pieces (streaming equals one pass, conv vs direct
@@ -60,13 +61,21 @@ int orc_conv1d_stream(int cin, int cout, int k, int stride, int dil, int replica
       xc[(size_t)c * total + ctx + i] = elu ? orc_elu(v) : v;
     }
   }
+  /* Chunks of floor(1024 / k) input channels: each an FMA chain from zero over its (channel,
+   * tap) terms in order, the chunks' sums then added in order (a fixed blocking of the
+   * reduction, as a blocked matmul has; it depends on the layer's shape only). */
+  const int cpc = 1024 / k > 0 ? 1024 / k : 1;
   for (int o = 0; o < cout; o++)
     for (int l = 0; l < len; l++) {
-      float acc = 0.0f;
-      for (int c = 0; c < cin; c++)
-        for (int j = 0; j < k; j++)
-          acc = fmaf(w[((size_t)o * cin + c) * k + j], xc[(size_t)c * total + (size_t)l * stride + (size_t)j * dil], acc);
-      float v = acc;
+      float v = 0.0f;
+      for (int c0 = 0; c0 < cin; c0 += cpc) {
+        float acc = 0.0f;
+        const int c1 = c0 + cpc < cin ? c0 + cpc : cin;
+        for (int c = c0; c < c1; c++)
+          for (int j = 0; j < k; j++)
+            acc = fmaf(w[((size_t)o * cin + c) * k + j], xc[(size_t)c * total + (size_t)l * stride + (size_t)j * dil], acc);
+        v = c0 == 0 ? acc : v + acc;
+      }
       if (bias) v = v + bias[o];
       if (skip) v = skip[(size_t)o * len + l] + v;
       out[(size_t)o * len + l] = v;
@@ -98,8 +107,14 @@ int orc_convtr1d_stream(int cin, int cout, int k, int stride, int depthwise, con
         if (depthwise) {
           p = w[(size_t)o * k + tap] * xa[(size_t)o * t + step];
         } else {
+          /* The taps' products are a 1x1 convolution: chunks of 1024 input channels. */
           p = 0.0f;
-          for (int c = 0; c < cin; c++) p = fmaf(w[((size_t)c * cout + o) * k + tap], xa[(size_t)c * t + step], p);
+          for (int c0 = 0; c0 < cin; c0 += 1024) {
+            float acc = 0.0f;
+            const int c1 = c0 + 1024 < cin ? c0 + 1024 : cin;
+            for (int c = c0; c < c1; c++) acc = fmaf(w[((size_t)c * cout + o) * k + tap], xa[(size_t)c * t + step], acc);
+            p = c0 == 0 ? acc : p + acc;
+          }
         }
         v = v + p;
       }

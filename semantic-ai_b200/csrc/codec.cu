@@ -114,7 +114,8 @@ __device__ __forceinline__ float conv_in(const ConvArgs& a, int b, int c, int i,
 // output is one FMA chain over (channel, tap) in order.
 constexpr int kConvTile = 64;
 
-__global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvArgs a, int cc_max, int nb) {
+__global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvArgs a, int cc_max, int nb, int cpc,
+                                                             float* partial) {
   constexpr int T = kConvTile, G = T / 4;
   extern __shared__ __align__(16) float sm[];
   float* ws = sm;                      // [cc_max * k][T]
@@ -122,13 +123,19 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvArgs a, 
   const int o0 = blockIdx.y * T, q0 = blockIdx.x * T, ncol = nb * a.len;
   const int tid = threadIdx.x, og = tid % G, cg = tid / G;
   const int total = a.ctx + a.t;
-  float acc[4][4];
+  // The reduction in chunks of cpc input channels (kConvChunkTerms / k): this CTA sums every
+  // chunk in order (partial null), or only chunk blockIdx.z into `partial`.
+  const int nchunks = (a.cin + cpc - 1) / cpc;
+  const int z0 = partial ? blockIdx.z : 0, z1 = partial ? blockIdx.z + 1 : nchunks;
+  float acc[4][4], sum[4][4];
+  for (int z = z0; z < z1; z++) {
 #pragma unroll
   for (int u = 0; u < 4; u++)
 #pragma unroll
     for (int i = 0; i < 4; i++) acc[u][i] = 0.f;
-  for (int c0 = 0; c0 < a.cin; c0 += cc_max) {
-    const int cc = min(cc_max, a.cin - c0), ck = cc * a.k;
+  const int cz1 = min(a.cin, (z + 1) * cpc);
+  for (int c0 = z * cpc; c0 < cz1; c0 += cc_max) {
+    const int cc = min(cc_max, cz1 - c0), ck = cc * a.k;
     __syncthreads();
     for (int i = tid; i < ck * T; i += kConvThreads) {
       const int r = i / T, o = i - r * T;
@@ -171,6 +178,11 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvArgs a, 
     }
   }
 #pragma unroll
+  for (int u = 0; u < 4; u++)
+#pragma unroll
+    for (int i = 0; i < 4; i++) sum[u][i] = z == z0 ? acc[u][i] : __fadd_rn(sum[u][i], acc[u][i]);
+  }  // chunks
+#pragma unroll
   for (int i = 0; i < 4; i++) {
     const int q = q0 + 4 * cg + i;
     if (q >= ncol) continue;
@@ -179,7 +191,11 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const ConvArgs a, 
     for (int u = 0; u < 4; u++) {
       const int o = o0 + 4 * og + u;
       if (o >= a.cout) continue;
-      float v = acc[u][i];
+      if (partial) {  // this chunk's sum, combined in chunk order by conv_combine_kernel
+        partial[((int64_t)blockIdx.z * nb * a.cout + (int64_t)b * a.cout + o) * a.len + l] = sum[u][i];
+        continue;
+      }
+      float v = sum[u][i];
       if (a.bias) v = __fadd_rn(v, a.bias[o]);  // matmul, then broadcast_add of the bias
       const int64_t off = b * a.o_bs + (int64_t)o * a.o_cs + l;
       if (a.skip) v = __fadd_rn(a.skip[off], v);  // ResnetBlock: xs + ys
@@ -198,6 +214,20 @@ __global__ void conv_state_kernel(const ConvArgs a, int nb) {
   const bool started = a.started[a.b0 + b] != 0;
   float* row = a.prev + ((int64_t)(a.b0 + b) * a.cin + c) * a.ctx;
   for (int u = 0; u < a.ctx; u++) row[u] = conv_in(a, b, c, a.t + u, started);
+}
+
+// The chunks' sums of a split convolution added in chunk order, then the bias and the skip.
+__global__ void conv_combine_kernel(const ConvArgs a, const float* partial, int nchunks, int nb) {
+  const int64_t n = (int64_t)nb * a.cout * a.len;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int l = (int)(i % a.len), o = (int)((i / a.len) % a.cout), b = (int)(i / ((int64_t)a.len * a.cout));
+  float v = partial[i];
+  for (int z = 1; z < nchunks; z++) v = __fadd_rn(v, partial[(int64_t)z * n + i]);
+  if (a.bias) v = __fadd_rn(v, a.bias[o]);
+  const int64_t off = b * a.o_bs + (int64_t)o * a.o_cs + l;
+  if (a.skip) v = __fadd_rn(a.skip[off], v);
+  a.out[off] = v;
 }
 
 // One StreamingConvTranspose1d::forward (nn/conv.rs:265-335) over nb streams: outputs
@@ -462,7 +492,7 @@ struct ConvLayer {
 
 // A step of a SEANet / codec pipeline: layer `layer` reads buffer `in` and writes `out` (both
 // channel-first; buffer ids below), with ELU on its input and an optional resnet skip.
-enum Buf { BUF_IN = 0, BUF_A = 1, BUF_B = 2, BUF_H = 3, BUF_OUT = 4, BUF_T = 5, BUF_P = 6, BUF_L = 7 };
+enum Buf { BUF_IN = 0, BUF_A = 1, BUF_B = 2, BUF_H = 3, BUF_OUT = 4, BUF_T = 5, BUF_P = 6, BUF_L = 7, BUF_S = 8 };
 struct ConvStep {
   int layer, in, out, act, skip;  // skip: a buffer id or -1
 };
@@ -493,8 +523,9 @@ struct CodecState {
   int max_batch = 0, max_frames = 0;
   DevBuf conv_state;           // [layer block][stream][...]
   DevBuf enc_started, dec_started;
-  DevBuf buf[6];  // blocks A, B, H, T, the transposed convolutions' products P, projected latents L
-  int64_t buf_floats[6] = {0, 0, 0, 0, 0, 0};
+  DevBuf buf[7];  // blocks A, B, H, T, transposed-convolution products P, projected latents L,
+                  // split-convolution partial sums S
+  int64_t buf_floats[7] = {0, 0, 0, 0, 0, 0, 0};
   State* enc_ts = nullptr;
   State* dec_ts = nullptr;
   ~CodecState() {
@@ -761,15 +792,34 @@ struct View {
   int64_t bs() const { return (int64_t)C * rowlen; }
 };
 
-void launch_conv(const ConvArgs& a, int nb, cudaStream_t st) {
+// Input channels per chunk of a convolution's reduction: the (channel, tap) terms are summed
+// in chunks of at most kConvChunkTerms (one FMA chain each), the chunks' sums in order. The
+// blocking depends on the layer's shape only, so results do not depend on the batch or the
+// launch; the CPU oracle sums the same way.
+constexpr int kConvChunkTerms = 1024;
+int conv_chunk_channels(int k) { return std::max(1, kConvChunkTerms / k); }
+int conv_chunks(int cin, int k) { return (cin + conv_chunk_channels(k) - 1) / conv_chunk_channels(k); }
+
+// scratch: nchunks * nb * cout * len floats when the layer has more than one chunk.
+void launch_conv(const ConvArgs& a, int nb, cudaStream_t st, float* scratch = nullptr) {
   // Input channels per stage: both operands' rows, 2 x 64 floats per (channel, tap).
   const int per_channel = 2 * kConvTile * a.k * 4;
-  const int cc = std::max(1, std::min(a.cin, kConvSmem / per_channel));
+  const int cpc = conv_chunk_channels(a.k);
+  const int cc = std::max(1, std::min({a.cin, cpc, kConvSmem / per_channel}));
   const size_t smem = (size_t)cc * per_channel;
   if (smem > (size_t)kConvSmem) throw Error(SVL_ERR_UNSUPPORTED, "convolution kernel too wide for one tile");
   const int64_t ncol = (int64_t)nb * a.len;
-  const dim3 grid((unsigned)((ncol + kConvTile - 1) / kConvTile), (a.cout + kConvTile - 1) / kConvTile);
-  conv1d_kernel<<<grid, kConvThreads, smem, st>>>(a, cc, nb);
+  const int nchunks = conv_chunks(a.cin, a.k);
+  const int tiles = (int)(((ncol + kConvTile - 1) / kConvTile) * ((a.cout + kConvTile - 1) / kConvTile));
+  // Few tiles (short chunks of a batch): one CTA per (tile, chunk), then the combine.
+  const bool split = nchunks > 1 && scratch && tiles < 148;
+  const dim3 grid((unsigned)((ncol + kConvTile - 1) / kConvTile), (a.cout + kConvTile - 1) / kConvTile,
+                  split ? nchunks : 1);
+  conv1d_kernel<<<grid, kConvThreads, smem, st>>>(a, cc, nb, cpc, split ? scratch : nullptr);
+  if (split) {
+    const int64_t n = (int64_t)nb * a.cout * a.len;
+    conv_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a, scratch, nchunks, nb);
+  }
   if (a.ctx > 0) conv_state_kernel<<<(nb * a.cin + 255) / 256, 256, 0, st>>>(a, nb);
 }
 
@@ -786,12 +836,12 @@ struct Exec {
   CodecState& S;
   int nb;
   bool dry;
-  int64_t need[6] = {0, 0, 0, 0, 0, 0};
+  int64_t need[7] = {0, 0, 0, 0, 0, 0, 0};
   cudaStream_t st;
   const int* started;
 
   float* buf(int id, int64_t floats) {
-    const int i = id == BUF_A ? 0 : id == BUF_B ? 1 : id == BUF_H ? 2 : id == BUF_P ? 4 : id == BUF_L ? 5 : 3;  // BUF_T: 3
+    const int i = id == BUF_A ? 0 : id == BUF_B ? 1 : id == BUF_H ? 2 : id == BUF_P ? 4 : id == BUF_L ? 5 : id == BUF_S ? 6 : 3;  // BUF_T: 3
     need[i] = std::max(need[i], floats);
     if (dry) return nullptr;
     if (floats > S.buf_floats[i]) throw Error(SVL_ERR_INVALID_INPUT, "codec call larger than the state's max_frames");
@@ -824,6 +874,9 @@ struct Exec {
     }
     // A transposed convolution's taps: products [b][cout * k][t] in block P.
     float* prod = L.tr && !L.depthwise ? buf(BUF_P, (int64_t)L.cout * L.k * in.t * nb) : nullptr;
+    // A convolution of several reduction chunks: room for the chunks' sums (block S).
+    const int nchunks = L.tr ? 1 : conv_chunks(L.cin, L.k);
+    float* scratch = nchunks > 1 ? buf(BUF_S, (int64_t)nchunks * nb * L.cout * out.t) : nullptr;
     if (dry) return out;
     if (L.tr) {
       if (!L.depthwise) {
@@ -892,7 +945,7 @@ struct Exec {
       a.o_bs = out.bs();
       a.o_cs = out.rowlen;
       a.len = out.t;
-      launch_conv(a, nb, st);
+      launch_conv(a, nb, st, scratch);
     }
     check_cuda(cudaGetLastError(), "codec convolution launch");
     return out;
@@ -1017,17 +1070,17 @@ CodecState* create_codec_state(Codec* c, int max_batch, int max_frames) {
     S->max_batch = max_batch;
     S->max_frames = max_frames;
     // Size the work blocks by a dry run of the largest call of each half.
-    int64_t need[6] = {0, 0, 0, 0, 0, 0};
+    int64_t need[7] = {0, 0, 0, 0, 0, 0, 0};
     for (int half = 0; half < 2; half++) {
       if (half == 0 && !c->enc_tr) continue;
       if (half == 1 && !c->dec_tr) continue;
-      Exec E{*S, max_batch, true, {0, 0, 0, 0, 0, 0}, c->stream, nullptr};
+      Exec E{*S, max_batch, true, {0, 0, 0, 0, 0, 0, 0}, c->stream, nullptr};
       if (half == 0) encode(E, max_frames, nullptr, nullptr);
       else if (c->latent_proj >= 0) decode_latent(E, max_frames, nullptr, nullptr, nullptr, nullptr);
       else decode(E, max_frames, nullptr, nullptr);
-      for (int i = 0; i < 6; i++) need[i] = std::max(need[i], E.need[i]);
+      for (int i = 0; i < 7; i++) need[i] = std::max(need[i], E.need[i]);
     }
-    for (int i = 0; i < 6; i++) {
+    for (int i = 0; i < 7; i++) {
       S->buf_floats[i] = need[i];
       if (need[i] > 0) S->buf[i].alloc(need[i] * 4);
     }
@@ -1243,7 +1296,7 @@ SVL_API svl_status svl_mimi_encode_step_device(svl_mimi* mimi, svl_mimi_state* s
     if (frames < 1 || frames > S.max_frames) throw Error(SVL_ERR_INVALID_INPUT, "frames must be 1..max_frames");
     svl::check_cuda(cudaSetDevice(mimi->c->device), "cudaSetDevice");
     cudaStream_t st = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : mimi->c->stream;
-    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0, 0}, st, S.enc_started.as<int>()};
+    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0, 0, 0}, st, S.enc_started.as<int>()};
     svl::encode(E, frames, d_pcm, d_latent);
     svl::mark_started_kernel<<<(batch + 255) / 256, 256, 0, st>>>(S.enc_started.as<int>(), batch);
     svl::check_cuda(cudaGetLastError(), "encode");
@@ -1261,7 +1314,7 @@ SVL_API svl_status svl_mimi_decode_step_device(svl_mimi* mimi, svl_mimi_state* s
     if (frames < 1 || frames > S.max_frames) throw Error(SVL_ERR_INVALID_INPUT, "frames must be 1..max_frames");
     svl::check_cuda(cudaSetDevice(mimi->c->device), "cudaSetDevice");
     cudaStream_t st = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : mimi->c->stream;
-    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0, 0}, st, S.dec_started.as<int>()};
+    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0, 0, 0}, st, S.dec_started.as<int>()};
     svl::decode(E, frames, d_latent, d_pcm);
     svl::mark_started_kernel<<<(batch + 255) / 256, 256, 0, st>>>(S.dec_started.as<int>(), batch);
     svl::check_cuda(cudaGetLastError(), "decode");
@@ -1283,7 +1336,7 @@ SVL_API svl_status svl_mimi_decode_latent_device(svl_mimi* mimi, svl_mimi_state*
     if (frames < 1 || frames > S.max_frames) throw Error(SVL_ERR_INVALID_INPUT, "frames must be 1..max_frames");
     svl::check_cuda(cudaSetDevice(mimi->c->device), "cudaSetDevice");
     cudaStream_t st = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : mimi->c->stream;
-    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0, 0}, st, S.dec_started.as<int>()};
+    svl::Exec E{S, batch, false, {0, 0, 0, 0, 0, 0, 0}, st, S.dec_started.as<int>()};
     svl::decode_latent(E, frames, d_latent, d_emb_std, d_emb_mean, d_pcm);
     svl::mark_started_kernel<<<(batch + 255) / 256, 256, 0, st>>>(S.dec_started.as<int>(), batch);
     svl::check_cuda(cudaGetLastError(), "decode");

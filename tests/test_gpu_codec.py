@@ -1,7 +1,7 @@
 """Mimi and the residual vector quantizer on the GPU against the oracle, through the C ABI.
 
 Each stream of a batch is compared with the oracle run on that stream alone. The convolutions
-run in the oracle's order (one FMA chain per output), so they match it to rounding; the
+sum in the oracle's order (fixed chunks of FMA chains per output), so they match it; the
 transformers between them sum attention in parallel, so the bar is relative: max |gpu - oracle|
 <= 1e-4 of the output's scale. The quantizer is compared bit for bit on the same latents; on
 latents that went through the encoder, a code may differ only where the oracle's two candidates
