@@ -3,8 +3,13 @@
 // Replaces the reference's CPU kernel (nn/kernels/attention.rs:81-169) and its generic
 // masked fallback on CUDA (nn/transformer.rs:346-364) for one new query per stream: query p
 // sees keys p - min(p + 1, window) + 1 .. p (first_key of the reference's compacting cache
-// is implied by the ring). The keys of a (stream, head) are split into `splits` chunks, one
-// CTA each; the chunks of a (stream, head) form one thread-block cluster.
+// is implied by the ring). Three kernels, by the number of (stream, head) units:
+//  - attn_flat_kernel (few units, short windows: batch 1 of the STT models): flat chunks of
+//    at most 48 keys, two CTAs per SM, keys loaded into registers, merged by the last CTA;
+//  - attn_kernel (few units, longer windows): the keys of a (stream, head) are split into
+//    `splits` chunks, one CTA each; the chunks of a (stream, head) form one thread-block
+//    cluster (described below);
+//  - attn_warp_kernel + attn_merge_kernel (148 units or more): pieces of keys per warp.
 //
 // Every key but the newest was written by an earlier step, and the in-projection of this
 // step only writes the newest slot, so each CTA bulk-copies its chunk's keys and values into
@@ -309,6 +314,223 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const AttnParams p) {
     }
     p.out[bh * HD + tid] = LL > 0.f ? AA / LL : 0.f;
   }
+}
+
+// ---- few streams, short windows: flat chunks merged by the last CTA ---------------------
+//
+// At batch 1 one layer's keys and values (12.3 MB of f32 for STT-1b) have been pulled into L2
+// by the kernel two places earlier, and the cluster kernel above is bound by its chain of
+// latencies (cluster scheduling, staging, cluster barrier), not by HBM: it takes as long on
+// L2-resident data as on cold data. Here each (stream, head) unit's keys are cut into
+// p.splits flat chunks of at most kFlatMaxKeys keys, one CTA each (about two per SM), with no
+// cluster and no staging:
+//  - before the dependency wait each warp loads its keys' rows (every key but the newest,
+//    which the in-projection writes) straight into registers, lane i holding dims
+//    [i * DL, (i + 1) * DL) of a row;
+//  - after it, q and the newest key. The warp scores its keys (the lane's DL products, then a
+//    butterfly sum, which leaves the same value in every lane), takes their max and adds its
+//    keys in order; the CTA merges its warps in warp order and stores the chunk's partial
+//    (max, sum of weights, weighted values) in p.part;
+//  - the last CTA of the unit to finish (a ticket per unit, p.ticket) merges the unit's
+//    chunks in chunk order and writes the output, then clears the ticket for the next launch.
+// The merge orders are fixed, so the result does not depend on timing. Nothing here waits.
+constexpr int kFlatWarps = 8;
+constexpr int kFlatKeysPerWarp = 6;
+constexpr int kFlatMaxKeys = kFlatWarps * kFlatKeysPerWarp;  // keys per chunk at most
+constexpr int kFlatMaxSplits = 2 * 148;                         // chunks per unit at most
+
+// W 32-bit words of a key row per lane (DL dims of f32, or of bf16 pairs), loaded through L2.
+template <int W>
+__device__ __forceinline__ void ld_row_words(const uint8_t* src, uint32_t (&w)[W]) {
+  if constexpr (W == 4) {
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src));
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (W == 2) {
+    const uint2 v = __ldcg(reinterpret_cast<const uint2*>(src));
+    w[0] = v.x; w[1] = v.y;
+  } else {
+    w[0] = __ldcg(reinterpret_cast<const unsigned int*>(src));
+  }
+}
+template <int DL, bool BF16, int W>
+__device__ __forceinline__ float row_dim(const uint32_t (&w)[W], int i) {
+  if (BF16) return (i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]);
+  return __uint_as_float(w[i]);
+}
+
+template <int HD, bool BF16>
+__global__ void __launch_bounds__(kFlatWarps * 32, 3) attn_flat_kernel(const AttnParams p) {
+  constexpr int DL = HD / 32;           // dims per lane
+  constexpr int EL = BF16 ? 2 : 4;
+  constexpr int W = DL * EL / 4;        // 32-bit words per lane per row
+  constexpr int ROW = HD * EL;
+  constexpr int KPW = kFlatKeysPerWarp;
+  constexpr int PS = HD + 4;            // floats per partial: values, then max and sum
+  __shared__ float sm_m[kFlatWarps], sm_l[kFlatWarps];
+  __shared__ float sm_a[kFlatWarps][HD];
+  __shared__ float fl_m[kFlatMaxSplits], fl_l[kFlatMaxSplits];  // the last CTA's merge
+  __shared__ bool last;
+
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = p.splits;
+  const int pos = p.pos[b];  // advanced only by the last kernel of a step
+  const int count = p.window > 0 ? min(pos + 1, p.window) : pos + 1;
+  const int kps = (count + S - 1) / S;
+  const int j0 = min(split * kps, count), j1 = min(j0 + kps, count);
+  const int first_pos = pos - count + 1;
+  const int kvh = h / (p.heads / p.kv_heads);
+  const int64_t head_base = (b * p.ring_stream_stride + (int64_t)kvh * p.ring_cap * HD) * EL;
+  const uint8_t* kg = static_cast<const uint8_t*>(p.k_ring) + head_base + lane * DL * EL;
+  const uint8_t* vg = static_cast<const uint8_t*>(p.v_ring) + head_base + lane * DL * EL;
+  auto row_off = [&](int j) {
+    const int q = first_pos + j;
+    return (int64_t)(p.window > 0 ? q % p.ring_cap : q) * ROW;
+  };
+
+  // Key r of this warp: j0 + warp + r * kFlatWarps.
+  uint32_t kw[KPW][W], vw[KPW][W];
+#pragma unroll
+  for (int r = 0; r < KPW; r++) {
+    const int j = j0 + warp + r * kFlatWarps;
+    if (j < j1 && j != count - 1) {
+      ld_row_words<W>(kg + row_off(j), kw[r]);
+      ld_row_words<W>(vg + row_off(j), vw[r]);
+    }
+  }
+  if (tid == 0) {
+    const int cta = split + S * (h + p.heads * b), ctas = S * p.heads * p.nb;
+    for (int i = 0; i < kMaxPrefetch; i++) prefetch_l2_share(p.pf[i].p, p.pf[i].bytes, cta, ctas);
+  }
+  pdl_launch();
+  pdl_wait();
+
+#pragma unroll
+  for (int r = 0; r < KPW; r++) {
+    const int j = j0 + warp + r * kFlatWarps;
+    if (j < j1 && j == count - 1) {
+      ld_row_words<W>(kg + row_off(j), kw[r]);
+      ld_row_words<W>(vg + row_off(j), vw[r]);
+    }
+  }
+  const int64_t unit = (int64_t)b * p.heads + h;
+  float q[DL];
+  {
+    uint32_t qw[DL];
+    ld_row_words<DL>(reinterpret_cast<const uint8_t*>(p.q + unit * HD + lane * DL), qw);
+#pragma unroll
+    for (int i = 0; i < DL; i++) q[i] = __uint_as_float(qw[i]);
+  }
+  float sc[KPW];
+#pragma unroll
+  for (int r = 0; r < KPW; r++) {
+    float d = 0.f;
+#pragma unroll
+    for (int i = 0; i < DL; i++) d = fmaf(q[i], row_dim<DL, BF16, W>(kw[r], i), d);
+    sc[r] = d;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < KPW; r++) sc[r] += __shfl_xor_sync(0xffffffffu, sc[r], o);
+  float m = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < KPW; r++) {
+    const bool valid = j0 + warp + r * kFlatWarps < j1;
+    sc[r] = valid ? p.scale * sc[r] : -INFINITY;  // scale * dot(q, k), as the reference
+    m = fmaxf(m, sc[r]);
+  }
+  float l = 0.f, acc[DL];
+#pragma unroll
+  for (int i = 0; i < DL; i++) acc[i] = 0.f;
+  if (m != -INFINITY) {
+#pragma unroll
+    for (int r = 0; r < KPW; r++) {
+      if (sc[r] == -INFINITY) continue;
+      const float e = exp_ref(sc[r] - m);
+      l = l + e;
+#pragma unroll
+      for (int i = 0; i < DL; i++) acc[i] = acc[i] + e * row_dim<DL, BF16, W>(vw[r], i);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < DL; i++) sm_a[warp][lane * DL + i] = acc[i];
+  if (lane == 0) {
+    sm_m[warp] = m;
+    sm_l[warp] = l;
+  }
+  __syncthreads();
+
+  // The chunk's partial: thread t < HD merges dim t of the warps, in warp order.
+  float A = 0.f, L = 0.f, M = -INFINITY;
+  if (tid < HD) {
+#pragma unroll
+    for (int w = 0; w < kFlatWarps; w++) M = fmaxf(M, sm_m[w]);
+    if (M != -INFINITY)
+#pragma unroll
+      for (int w = 0; w < kFlatWarps; w++) {
+        if (sm_m[w] == -INFINITY) continue;
+        const float c = exp_ref(sm_m[w] - M);
+        L = L + sm_l[w] * c;
+        A = A + sm_a[w][tid] * c;
+      }
+  }
+  if (S == 1) {
+    if (tid < HD) p.out[unit * HD + tid] = L > 0.f ? A / L : 0.f;
+    return;
+  }
+  float* part = p.part + (unit * S + split) * PS;
+  if (tid < HD) {
+    part[tid] = A;
+    if (tid == 0) {
+      part[HD] = M;
+      part[HD + 1] = L;
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(p.ticket + unit, 1u) == (unsigned)S - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // The unit's chunks in chunk order. Dim t of the first 32 chunks (thread t < HD), and every
+  // chunk's max and sum (one thread per chunk), are loaded at once; then each chunk's scale
+  // exp(max_s - max) (0 for an empty chunk); further chunks come 32 per round trip.
+  const float* up = p.part + unit * S * PS;
+  constexpr int kU = 32;
+  float a[kU];
+  if (tid < HD) {
+#pragma unroll
+    for (int u = 0; u < kU; u++) a[u] = u < S ? __ldcg(up + (int64_t)u * PS + tid) : 0.f;
+  }
+  for (int i = tid; i < S; i += kFlatWarps * 32) {
+    fl_m[i] = __ldcg(up + (int64_t)i * PS + HD);
+    fl_l[i] = __ldcg(up + (int64_t)i * PS + HD + 1);
+  }
+  __syncthreads();
+  float MM = -INFINITY;
+  for (int i = 0; i < S; i++) MM = fmaxf(MM, fl_m[i]);
+  __syncthreads();
+  for (int i = tid; i < S; i += kFlatWarps * 32) fl_m[i] = fl_m[i] == -INFINITY ? 0.f : exp_ref(fl_m[i] - MM);
+  __syncthreads();
+  if (tid < HD) {
+    float LL = 0.f, AA = 0.f;
+    for (int s0 = 0; s0 < S; s0 += kU) {
+      if (s0 > 0) {
+#pragma unroll
+        for (int u = 0; u < kU; u++) a[u] = s0 + u < S ? __ldcg(up + (int64_t)(s0 + u) * PS + tid) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kU; u++) {
+        if (s0 + u >= S) break;
+        const float c = fl_m[s0 + u];
+        LL = LL + fl_l[s0 + u] * c;
+        AA = AA + a[u] * c;
+      }
+    }
+    p.out[unit * HD + tid] = LL > 0.f ? AA / LL : 0.f;
+  }
+  if (tid == 0) p.ticket[unit] = 0u;
 }
 
 // ---- many streams: pieces of a fixed key count -----------------------------------------
@@ -888,6 +1110,20 @@ void launch_t(const AttnParams& p, cudaStream_t s) {
 }
 
 template <int HD, bool BF16>
+void launch_f(const AttnParams& p, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits, p.heads, p.nb);
+  cfg.blockDim = dim3(kFlatWarps * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, attn_flat_kernel<HD, BF16>, p);
+}
+
+template <int HD, bool BF16>
 void set_attr() {
   cudaFuncSetAttribute(attn_kernel<HD, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        128 + 2 * kSlots * kTileBytes);
@@ -898,6 +1134,8 @@ void set_attr() {
 }  // namespace
 
 int attention_max_splits() { return kMaxSplits; }
+
+int attention_flat_max_keys() { return kFlatMaxKeys; }
 
 void attention_init_device() {
   set_attr<64, false>();
@@ -917,6 +1155,16 @@ int attention_piece(int head_dim, int kv_bf16, int ring_cap, int* npieces) {
 }
 
 void launch_attention_decode(const AttnParams& p, cudaStream_t s) {
+  // Few streams, short windows: flat chunks (p.ticket set at state creation).
+  if (p.ticket) {
+    switch (p.head_dim * 2 + p.kv_bf16) {
+      case 128: launch_f<64, false>(p, s); return;
+      case 129: launch_f<64, true>(p, s); return;
+      case 256: launch_f<128, false>(p, s); return;
+      case 257: launch_f<128, true>(p, s); return;
+      default: return;  // rejected at model creation
+    }
+  }
   if (p.splits == 1 && p.part) {
     // Enough (stream, head) units to cover the GPU: pieces handed out to warps (up to the
     // stream count whose item prefix fits in shared memory).

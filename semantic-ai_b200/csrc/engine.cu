@@ -425,6 +425,19 @@ State* create_state(Model* m, int max_batch, int max_positions, uint32_t flags) 
     int splits = (148 + units - 1) / units;
     splits = std::max(1, std::min({splits, (s->cap + 15) / 16, attention_max_splits()}));
     s->splits = splits;
+    if (splits > 1) {
+      // Few streams: when every chunk fits attn_flat_kernel's keys per CTA at about two CTAs
+      // per SM (at least 8 keys per chunk), flat chunks replace the clusters.
+      int fs = std::max(1, 2 * 148 / units);
+      fs = std::min(fs, (s->cap + 7) / 8);
+      if (fs > 1 && (s->cap + fs - 1) / fs <= attention_flat_max_keys()) {
+        s->attn_flat = true;
+        s->splits = fs;
+        s->attn_part.alloc((int64_t)units * fs * (c.head_dim + 4) * 4);
+        s->attn_ticket.alloc((int64_t)units * 4);
+        check_cuda(cudaMemsetAsync(s->attn_ticket.p, 0, s->attn_ticket.bytes, m->stream), "memset");
+      }
+    }
     if (splits == 1) {
       // Many streams: pieces of keys spread over the warps, partials merged per unit.
       s->piece = attention_piece(c.head_dim, s->kv_elt == 2, s->cap, &s->npieces);
@@ -672,6 +685,10 @@ LayerParams layer_params(Model& m, State& s, int l, int b0, int nb) {
   a.piece = s.piece;
   a.npieces = s.npieces;
   a.part = s.attn_part.as<float>();
+  if (s.attn_flat) {
+    a.part += (int64_t)b0 * c.num_heads * s.splits * (hd + 4);
+    a.ticket = s.attn_ticket.as<unsigned>() + (int64_t)b0 * c.num_heads;
+  }
   a.kmap = s.ring_maps ? s.kmap : nullptr;
   a.vmap = s.ring_maps ? s.vmap : nullptr;
   a.layer = l;

@@ -143,6 +143,10 @@ struct State {
   // partials of the units of several pieces.
   int piece = 0, npieces = 0;
   DevBuf attn_part;
+  // Few streams with short windows: flat chunks merged by the last CTA of each unit (the
+  // tickets, [max_batch][heads], zero between launches; partials in attn_part).
+  bool attn_flat = false;
+  DevBuf attn_ticket;
   alignas(64) unsigned char kmap[128], vmap[128];  // bf16 rings as TMA tensors
   bool ring_maps = false;
   // Tensor-core path (bf16 weights, many streams): bf16 operand rows and their TMA maps, per

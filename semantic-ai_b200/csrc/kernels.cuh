@@ -145,6 +145,9 @@ struct AttnParams {
   // [nb][heads][npieces][head_dim + 4] of the units of several pieces.
   int piece, npieces;
   float* part;
+  // Few streams (attn_flat_kernel, when set): one ticket per (stream, head) unit, zero between
+  // launches, and the chunks' partials [nb][heads][splits][head_dim + 4] in `part`.
+  unsigned* ticket;
   // Tensor-map view of bf16 rings (make_ring_map): host copies of the maps of k_ring's and
   // v_ring's whole allocations, this layer's index in them, and the map row of stream 0's slot 0.
   const unsigned char* kmap;
@@ -155,6 +158,8 @@ struct AttnParams {
 
 void launch_attention_decode(const AttnParams& p, cudaStream_t s);
 int attention_max_splits();
+// Keys per chunk at most of the flat few-stream attention (attn_flat_kernel).
+int attention_flat_max_keys();
 // Keys per piece of the many-stream attention for a ring of `ring_cap` keys; *npieces = the
 // most pieces a (stream, head) can have.
 int attention_piece(int head_dim, int kv_bf16, int ring_cap, int* npieces);

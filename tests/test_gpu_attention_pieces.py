@@ -1,18 +1,19 @@
-"""Many-stream attention (pieces of keys handed out at run time) against a float64 reference
-and against the small-batch attention path.
+"""The three decode-attention kernels against a float64 reference and against each other.
 
 A batch state of 40 streams has at least 148 (stream, head) units, so its attention runs the
 many-stream kernel: the keys of each unit are cut into pieces, warps take pieces in a fixed
 round-robin order, and a follow-up kernel merges the partials of units of several pieces. Each
 stream is put at its own position with random imported caches (positions past the window wrap
-the ring), so units have 1 .. 10 pieces. The same streams in one-stream states run the
-cluster-split kernel. Checked for three consecutive steps (the partial buffers are reused by
-every launch):
+the ring), so units have 1 .. 10 pieces. The same streams in one-stream states run the flat
+few-stream kernel (chunks of at most 48 keys, merged by the last CTA of each unit), and the
+first 12 of them in one 12-stream state run the cluster-split kernel (4-CTA clusters of 75
+keys each). Checked for three consecutive steps (the partial buffers and the flat kernel's
+tickets are reused by every launch):
 - f32 caches: logits within 2e-3 max-abs of the float64 reference (the reference's step over
   the exported caches);
 - bf16 caches: within 2e-2 relative of it (the newest key is rounded to bf16 on the device);
-- both: the batch state within 1e-4 max-abs of the one-stream states (same inputs, different
-  attention kernels), and two runs of the batch state bit-identical.
+- both: the batch state within 1e-4 max-abs of the one-stream and the 12-stream states (same
+  inputs, different attention kernels), and two runs of the batch state bit-identical.
 """
 import numpy as np
 import pytest
@@ -67,6 +68,10 @@ def test_many_stream_attention_pieces(svl_lib, head_dim, kvdt):
     twin = gm.init_state(B)
     for b in range(B):
         twin.copy_from(singles[b], 0, b)
+    M = 12
+    mid = gm.init_state(M)
+    for b in range(M):
+        mid.copy_from(singles[b], 0, b)
     text = rng.integers(0, stt.text_card, size=(steps, B)).astype(np.uint32)
     audio = rng.integers(0, stt.card, size=(steps, B, stt.n_q)).astype(np.uint32)
     for i in range(steps):
@@ -74,10 +79,14 @@ def test_many_stream_attention_pieces(svl_lib, head_dim, kvdt):
         _, lg = gm.step(text[i], audio[i], big, logits=True)
         _, lg2 = gm.step(text[i], audio[i], twin, logits=True)
         np.testing.assert_array_equal(lg, lg2)
+        _, lm = gm.step(text[i][:M], audio[i][:M], mid, logits=True)
+        for b in range(M):
+            d = float(np.max(np.abs(lg[b] - lm[b])))
+            assert d <= 1e-4, f"step {i} stream {b} (position {positions[b] + i}): {d} from the cluster path"
         for b in range(B):
             _, ls = gm.step(text[i][b:b + 1], audio[i][b:b + 1], singles[b], logits=True)
             d = float(np.max(np.abs(lg[b] - ls[0])))
-            assert d <= 1e-4, f"step {i} stream {b} (position {positions[b] + i}): {d} from the split path"
+            assert d <= 1e-4, f"step {i} stream {b} (position {positions[b] + i}): {d} from the flat path"
             ref = reference_step(stt, cfg, w, exported[b], int(positions[b]) + i, int(text[i][b]),
                                  audio[i][b])
             if kvdt == "f32":
