@@ -339,7 +339,21 @@ constexpr int kFlatKeysPerWarp = 6;
 constexpr int kFlatMaxKeys = kFlatWarps * kFlatKeysPerWarp;  // keys per chunk at most
 constexpr int kFlatMaxSplits = 2 * 148;                         // chunks per unit at most
 
-// W 32-bit words of a key row per lane (DL dims of f32, or of bf16 pairs), loaded through L2.
+// W 32-bit words of a key row per lane (DL dims of f32, or of bf16 pairs), loaded through L2
+// with eviction policy `pol` (the window is read once per step, so its lines go first).
+template <int W>
+__device__ __forceinline__ void ld_row_words_hint(const uint8_t* src, uint32_t (&w)[W], uint64_t pol) {
+  if constexpr (W == 4) {
+    asm volatile("ld.global.cg.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                 : "l"(src), "l"(pol));
+  } else if constexpr (W == 2) {
+    asm volatile("ld.global.cg.L2::cache_hint.v2.u32 {%0, %1}, [%2], %3;" : "=r"(w[0]), "=r"(w[1]) : "l"(src), "l"(pol));
+  } else {
+    asm volatile("ld.global.cg.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(w[0]) : "l"(src), "l"(pol));
+  }
+}
+// The same without a policy.
 template <int W>
 __device__ __forceinline__ void ld_row_words(const uint8_t* src, uint32_t (&w)[W]) {
   if constexpr (W == 4) {
@@ -389,13 +403,14 @@ __global__ void __launch_bounds__(kFlatWarps * 32, 3) attn_flat_kernel(const Att
   };
 
   // Key r of this warp: j0 + warp + r * kFlatWarps.
+  const uint64_t pol = l2_evict_first();
   uint32_t kw[KPW][W], vw[KPW][W];
 #pragma unroll
   for (int r = 0; r < KPW; r++) {
     const int j = j0 + warp + r * kFlatWarps;
     if (j < j1 && j != count - 1) {
-      ld_row_words<W>(kg + row_off(j), kw[r]);
-      ld_row_words<W>(vg + row_off(j), vw[r]);
+      ld_row_words_hint<W>(kg + row_off(j), kw[r], pol);
+      ld_row_words_hint<W>(vg + row_off(j), vw[r], pol);
     }
   }
   if (tid == 0) {

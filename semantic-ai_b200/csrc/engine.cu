@@ -559,15 +559,18 @@ void set_norm(GemvParams& p, const Norm& N) {
 
 // L2 prefetches. A small-batch kernel that reads its data cold from HBM gets ~3.5 TB/s (a burst
 // of tens of KB per SM waits ~1.6 us for its first bytes); data prefetched into L2 shortly
-// before comes at ~6-7 TB/s, but is gone again after some 64 MB of other traffic (measured on
-// B200 with bulk copies of 96 KB per SM). So every kernel of the step pulls into L2 the data
-// of the kernel kPrefetchDistance places after it in the step's sequence -- per layer in_proj,
-// attention (the layer's K and V rings), out_proj, linear_in, linear_out, then the STT head --
-// counted cyclically, the next step's first kernels after the head. Measured per STT-1b q8_0
-// step at batch 1: 703 us at distance 2, 708 at 3, 734 at 5 (one layer ahead: evicted before
-// use), 755 at 8. A range is prefetched only when it takes at most a quarter of L2.
+// before comes at ~6-7 TB/s, but with plain accesses it is gone again after some 64 MB of
+// other traffic (measured on B200 with bulk copies of 96 KB per SM). So every kernel of the
+// step pulls into L2 the data of the kernel kPrefetchDistance places after it in the step's
+// sequence -- per layer in_proj, attention (the layer's K and V rings), out_proj, linear_in,
+// linear_out, then the STT head -- counted cyclically, the next step's first kernels after the
+// head. The prefetches carry an evict-last policy and the kernels' own reads of their weights
+// and keys an evict-first one, so the reads streaming through L2 in between no longer push the
+// prefetched lines out. Measured per STT-1b q8_0 step at batch 1 (full window): without the
+// policies 639 us at distance 2; with them 615 us at distance 2, 611 at 3, 616 at 4, 619 at 5.
+// A range is prefetched only when it takes at most a quarter of L2.
 constexpr int64_t kPrefetchMax = 32ll * 1024 * 1024;
-constexpr int kPrefetchDistance = 2;
+constexpr int kPrefetchDistance = 3;
 
 PrefetchRange weights_range(const Linear* L) {
   if (!L || L->row_stride * L->n > kPrefetchMax) return PrefetchRange{};

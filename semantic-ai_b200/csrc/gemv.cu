@@ -40,11 +40,13 @@ constexpr int kGrid = 148 * kCtasPerSm;
 // The argmax scratch (the state's and the no-allocation head's) holds one candidate per CTA.
 static_assert(kGrid <= kLogitsGrid, "the argmax scratch holds kLogitsGrid CTAs per stream");
 
-__device__ __forceinline__ uint4 ldg_weights(const void* p) {
+// 16 bytes of weights, read once per step: kept out of L1, evicted first from L2 (pol from
+// l2_evict_first()).
+__device__ __forceinline__ uint4 ldg_weights(const void* p, uint64_t pol) {
   uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
+               : "l"(p), "l"(pol));
   return r;
 }
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int j) {
@@ -172,6 +174,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
   const int g0 = (int)((int64_t)gw * groups / total_w), g1 = (int)((int64_t)(gw + 1) * groups / total_w);
 
   uint4 wv[R][U];
+  const uint64_t pol = l2_evict_first();
   // Loads chunks [c0, c0 + 32 U) of group g's rows: every load of the group is in flight at once.
   auto issue = [&](int g, int c0) {
 #pragma unroll
@@ -181,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
         const int c = c0 + lane + 32 * u;
         const int row = g * R + r;
         const bool on = g < g1 && c < nch && row < p.n;
-        wv[r][u] = on ? ldg_weights(p.w + (int64_t)row * p.row_stride + (int64_t)c * 16) : make_uint4(0, 0, 0, 0);
+        wv[r][u] = on ? ldg_weights(p.w + (int64_t)row * p.row_stride + (int64_t)c * 16, pol) : make_uint4(0, 0, 0, 0);
       }
   };
   issue(g0, 0);
@@ -374,12 +377,14 @@ __global__ void __launch_bounds__(kThreads, 3) qgemv_kernel(const GemvParams p, 
   // Group G0 + i into stage i % nst (the failure drill withholds CTA 0's first copy).
   const bool withhold = p.test_withhold && blockIdx.x == 0;
   const uint32_t limit = p.wait_limit ? p.wait_limit : kWaitLimit;
+  // The weights are read once per step: their L2 lines go first.
+  const uint64_t pol = l2_evict_first();
   auto copy_group = [&](int i) {
     if (withhold && i == 0) return;
     const int g = G0 + i, st = i % nst;
     const uint32_t bytes = (uint32_t)(min(4, p.n - 4 * g) * p.row_stride);
     mbar_expect_tx(&full[st], bytes);
-    bulk_g2s(stg + (size_t)st * gbytes, p.w + (int64_t)g * gbytes, bytes, &full[st]);
+    bulk_g2s_hint(stg + (size_t)st * gbytes, p.w + (int64_t)g * gbytes, bytes, &full[st], pol);
     issued[st]++;
   };
   if (tid == 0) {
@@ -501,6 +506,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) rgemv_kernel(const GemvP
   const int total_w = gridDim.x * kWarps;
   const int gw = blockIdx.x * kWarps + warp;
   const int g0 = (int)((int64_t)gw * groups / total_w), g1 = (int)((int64_t)(gw + 1) * groups / total_w);
+  const uint64_t pol = l2_evict_first();
   prefetch_share(p);
   NormPre pre;
   norm_preload<kThreads>(p, pre);
@@ -525,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) rgemv_kernel(const GemvP
       for (int u = 0; u < U; u++) {
         const int c = c0 + u;
         if (WT == W_F32) {
-          const uint4 v = on && c < nch ? ldg_weights(wrow + (int64_t)(16 * c + 4 * j) * 4) : make_uint4(0, 0, 0, 0);
+          const uint4 v = on && c < nch ? ldg_weights(wrow + (int64_t)(16 * c + 4 * j) * 4, pol) : make_uint4(0, 0, 0, 0);
           w[u][0] = __uint_as_float(v.x); w[u][1] = __uint_as_float(v.y);
           w[u][2] = __uint_as_float(v.z); w[u][3] = __uint_as_float(v.w);
         } else {

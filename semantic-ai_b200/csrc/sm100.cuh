@@ -51,17 +51,41 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
 }
-__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+// L2 eviction policies (createpolicy). A step streams ~1 GB through a 126 MB L2 at batch 1:
+// bytes a kernel reads once for itself go first, bytes pulled ahead for a later kernel go last,
+// so that the streaming reads in between do not push the prefetched lines out.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// bulk_g2s with an L2 eviction policy.
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes, uint64_t pol) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(pol)
+               : "memory");
 }
 // CTA `cta` of `ctas` pulls its 16-byte-aligned share of [base, base + bytes) into L2, in
-// pieces of at most 64 KB.
+// pieces of at most 64 KB, to be evicted last.
 __device__ __forceinline__ void prefetch_l2_share(const uint8_t* base, int64_t bytes, int cta, int ctas) {
   if (!base || bytes <= 0) return;
+  const uint64_t pol = l2_evict_last();
   const int64_t share = (bytes / ctas + 15) / 16 * 16;
   const int64_t a = (int64_t)cta * share;
   const int64_t e = min(a + share, bytes / 16 * 16);
-  for (int64_t o = a; o < e; o += 65536) prefetch_l2(base + o, (uint32_t)(e - o < 65536 ? e - o : 65536));
+  for (int64_t o = a; o < e; o += 65536) prefetch_l2(base + o, (uint32_t)(e - o < 65536 ? e - o : 65536), pol);
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
