@@ -150,6 +150,23 @@ def init_dist(world, local_rank):
     return dist
 
 
+def max_over_ranks(dist, x: float, device) -> float:
+    """The largest x over all ranks (x itself without a process group): every multi-GPU time
+    is the slowest rank's."""
+    if not dist:
+        return float(x)
+    import torch
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def rank_streams(rank: int, per_rank: int) -> range:
+    """The global indices of the streams rank `rank` runs: ranks shard the streams in contiguous
+    blocks of per_rank, so stream g's inputs (seeded by g) do not depend on the GPU count."""
+    return range(rank * per_rank, (rank + 1) * per_rank)
+
+
 def stt_spec_config(spec, layers):
     import dataclasses
     stt = preset(spec["preset"])
@@ -175,7 +192,7 @@ def measure_stt(args, spec, rank, world, local_rank, dist, weights=None, full=Tr
     dev = f"cuda:{local_rank}"
 
     # Per-stream audio: global stream g draws from seed 1 + g; frame 0 sees the initial tokens.
-    g0 = rank * B
+    g0 = rank_streams(rank, B).start
     audio = synth.audio_tokens(stt, K + W, seed=1 + g0, streams=B)
     rng = np.random.default_rng(2 + rank)
     if spec.get("stagger"):
@@ -243,10 +260,7 @@ def measure_stt(args, spec, rank, world, local_rank, dist, weights=None, full=Tr
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(dist, ms, dev)
     value = world * B * K / (ms_max / 1000.0)
     st.close()
 
@@ -268,10 +282,7 @@ def measure_stt(args, spec, rank, world, local_rank, dist, weights=None, full=Tr
     for i in range(K):
         prev = model.step(prev, aud[i], st)
     e2e_s = time.perf_counter() - t0
-    t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = world * B * K / float(t.item())
+    e2e_value = world * B * K / max_over_ranks(dist, e2e_s, dev)
     st.close()
 
     # Kernel families, timed on their launching stream with every stream at its mean fill of
@@ -415,7 +426,7 @@ def run_tts(args, spec, rank, world, local_rank):
     weights = synth.tts_weights(cfg, tts, seed=0)
     model = FlowLm(cfg, tts, weights, device=local_rank)
     L = _lib.lib()
-    g0 = rank * B
+    g0 = rank_streams(rank, B).start
     tokens = np.stack([np.random.default_rng(3 + g0 + b).integers(0, tts.text_bins, size=P, dtype=np.uint32)
                        for b in range(B)])
     noise = np.random.default_rng(4 + rank).standard_normal((K + W, B, tts.latent_dim)).astype(np.float32)
@@ -462,10 +473,7 @@ def run_tts(args, spec, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize()
     clk = clocks.stop()
-    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(dist, e0.elapsed_time(e1), dev)
     value = world * B * K / (ms_max / 1000.0)
     st.close()
 
@@ -478,10 +486,7 @@ def run_tts(args, spec, rank, world, local_rank):
     for i in range(K):
         prev, _ = model.step(prev, noise[i], st)
     e2e_s = time.perf_counter() - t0
-    t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = world * B * K / float(t.item())
+    e2e_value = world * B * K / max_over_ranks(dist, e2e_s, dev)
     st.close()
 
     # Kernel families: transformer products, attention (at the run's mean fill), flow head.
@@ -630,8 +635,8 @@ def measure_codec(args, spec, rank, world, local_rank, dist, K, W, cpu=True):
         w = synth.mimi_weights(cfg)
         if part == codec.ENCODER:
             w.update(synth.rvq_weights(32, 2048))
-        m = codec.Mimi(cfg, w)
-        q = codec.Quantizer(32, 2048, w) if part == codec.ENCODER else None
+        m = codec.Mimi(cfg, w, device=local_rank)
+        q = codec.Quantizer(32, 2048, w, device=local_rank) if part == codec.ENCODER else None
         st = m.init_state(B, 1)
         fs = m.frame_size
         g = torch.Generator(device="cuda").manual_seed(11 + rank)
@@ -659,10 +664,7 @@ def measure_codec(args, spec, rank, world, local_rank, dist, K, W, cpu=True):
             e1.record(stream)
             e1.synchronize()
         ms = e0.elapsed_time(e1) / K
-        if dist:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+        ms = max_over_ranks(dist, ms, "cuda")
         # End to end: the frame from pinned host memory, the result back to the host.
         host_in = [x.cpu().pin_memory() for x in ins[:4]]
         h2d = host_in[0].numel() * 4
@@ -678,6 +680,7 @@ def measure_codec(args, spec, rank, world, local_rank, dist, K, W, cpu=True):
                 y.cpu()
             stream.synchronize()
             e2e_ms = (time.perf_counter() - t0) * 1e3 / K
+        e2e_ms = max_over_ranks(dist, e2e_ms, "cuda")
         flops = codec_flops(cfg, part) * B
         leg = {"value": round(B * world * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
                "e2e": {"value": round(B * world * 1e3 / e2e_ms, 1), "unit": "stream-frames/s",
