@@ -222,6 +222,41 @@ void validate_cfg(const svl_transformer_config& c) {
 
 }  // namespace
 
+// The flow head's modulation products (each ResBlock's adaLN_modulation, then the final
+// layer's) read the same conditioning, so they run as one product: their packed rows and
+// biases are copied, in that order, into m.mods. Packed rows do not depend on the matrix they
+// belong to, and every part has a multiple of 4 rows, so the copy keeps the layout (and each
+// row's result) of the separate products. The parts stay loaded for their byte counts.
+static void stack_mods(Model& m) {
+  std::vector<const Linear*> parts;
+  for (const ResBlock& r : m.res) parts.push_back(&r.mod);
+  parts.push_back(&m.final_mod);
+  Linear& S = m.mods;
+  const Linear& f = *parts[0];
+  S.k = f.k;
+  S.wtype = f.wtype;
+  S.row_stride = f.row_stride;
+  S.n = 0;
+  for (const Linear* L : parts) {
+    if (L->k != S.k || L->wtype != S.wtype || L->row_stride != S.row_stride || L->n % 4 || !L->bias.p)
+      throw Error(SVL_ERR_CONFIG, "flow head modulation products differ in shape");
+    S.n += L->n;
+  }
+  S.w.alloc(S.row_stride * S.n);
+  S.bias.alloc((int64_t)S.n * 4);
+  int64_t row = 0;
+  for (const Linear* L : parts) {
+    check_cuda(cudaMemcpyAsync(S.w.as<uint8_t>() + row * S.row_stride, L->w.p, L->row_stride * L->n,
+                               cudaMemcpyDeviceToDevice, m.stream), "stack");
+    check_cuda(cudaMemcpyAsync(S.bias.as<float>() + row, L->bias.p, (size_t)L->n * 4, cudaMemcpyDeviceToDevice,
+                               m.stream), "stack");
+    row += L->n;
+  }
+  check_cuda(cudaStreamSynchronize(m.stream), "stack");
+  if (S.wtype == W_BF16 && !make_gemm_operand(S.tc, S.w.p, S.n, S.k, S.row_stride, 128))
+    throw Error(SVL_ERR_CUDA, "flow head modulation: cannot encode its TMA tensor map");
+}
+
 Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_config* stt,
                     const svl_tts_config* tts, const svl_tensor_view* t, int n, int device,
                     const char* prefix) {
@@ -317,6 +352,7 @@ Model* create_model(int kind, const svl_transformer_config& cfg, const svl_stt_c
                 "flow_net.final_layer.adaLN_modulation.1.bias", 2 * dim, dim, true);
       ld.linear(m->final_linear, "flow_net.final_layer.linear.weight",
                 "flow_net.final_layer.linear.bias", lat, dim, true);
+      stack_mods(*m);
     }
     check_cuda(cudaStreamSynchronize(m->stream), "load");
   } catch (...) {
@@ -511,7 +547,7 @@ State* create_state(Model* m, int max_batch, int max_positions, uint32_t flags) 
       s->hbuf.alloc(B * dim * 4);
       s->h2buf.alloc(B * dim * 4);
       s->xs2.alloc(B * dim * 4);
-      s->modbuf.alloc(B * 3 * dim * 4);
+      s->modbuf.alloc(B * m->mods.n * 4);
       s->temb_in.alloc(256 * 4);
       s->temb_h.alloc(dim * 4);
       s->temb_o.alloc(dim * 4);
@@ -1002,15 +1038,18 @@ void enqueue_flow(Model& m, State& s, int nb, int steps, const float* ttab, cuda
     launch_cond_silu(y, n_time > 0 ? ttab + (int64_t)i * dim : nullptr,
                      n_time > 0 ? (float)(1.0 / (double)n_time) : 0.f, dim, nb, sy, st);
     linear_fwd(m, s, m.input_proj, x, lat, nb, EPI_STORE, xs, dim, st);
-    for (const ResBlock& r : m.res) {
-      linear_fwd(m, s, r.mod, sy, dim, nb, EPI_STORE, mod, 3 * dim, st);
-      launch_adaln(xs, nb, dim, r.ln.w.as<float>(), r.ln.b.as<float>(), 1, r.ln.eps, mod, 3 * dim, hh, st);
+    // Every block's shift / scale / gate and the final layer's shift / scale in one product.
+    const int ms = m.mods.n;
+    linear_fwd(m, s, m.mods, sy, dim, nb, EPI_STORE, mod, ms, st);
+    for (size_t i = 0; i < m.res.size(); i++) {
+      const ResBlock& r = m.res[i];
+      const float* mi = mod + (int64_t)i * 3 * dim;
+      launch_adaln(xs, nb, dim, r.ln.w.as<float>(), r.ln.b.as<float>(), 1, r.ln.eps, mi, ms, hh, st);
       linear_fwd(m, s, r.mlp1, hh, dim, nb, EPI_SILU, h2, dim, st);
       linear_fwd(m, s, r.mlp2, h2, dim, nb, EPI_STORE, hh, dim, st);
-      launch_gate_add(xs, mod, 3 * dim, 2 * dim, hh, nb, dim, st);
+      launch_gate_add(xs, mi, ms, 2 * dim, hh, nb, dim, st);
     }
-    linear_fwd(m, s, m.final_mod, sy, dim, nb, EPI_STORE, mod, 2 * dim, st);
-    launch_adaln(xs, nb, dim, nullptr, nullptr, 0, 1e-6f, mod, 2 * dim, hh, st);
+    launch_adaln(xs, nb, dim, nullptr, nullptr, 0, 1e-6f, mod + (int64_t)m.res.size() * 3 * dim, ms, hh, st);
     linear_fwd(m, s, m.final_linear, hh, dim, nb, EPI_STORE, flow, lat, st);
     const int mode = n_time > 0 ? 0 : t.flow_kind == 2 ? 1 : 2;
     launch_flow_update(x, flow, (int64_t)nb * lat, mode, (float)(1.0 / (double)steps), st);

@@ -109,6 +109,10 @@ struct Model {
   std::vector<TimeEmbed> time_emb;
   Linear cond_embed, input_proj, final_mod, final_linear;
   std::vector<ResBlock> res;
+  // Every ResBlock's adaLN_modulation rows, then the final layer's, stacked into one product
+  // (they all read the same conditioning): rows [3 dim i, 3 dim (i + 1)) are block i's,
+  // the last 2 dim the final layer's.
+  Linear mods;
   int64_t weight_bytes = 0;
   bool shadows = false;  // quantised linears have bf16 images for the tensor-core path
   std::mutex shadow_mu;
